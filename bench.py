@@ -1,0 +1,337 @@
+"""Benchmark: SwiGLU MoE layer forward + backward on B200 (the reference's headline path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the largest single-GPU config of the headline metric):
+T=8192 tokens, d=4096, E=64 experts, top-2, H=11008, bf16 SwiGLU; router weight
+[4096, 64] ~ N(0, 0.02) on x ~ N(0, 1); expert weights ~ N(0, 0.02); grad_out ~ N(0, 1).
+A step = router GEMM + fused top-k softmax + permute + 3 grouped GEMMs + SwiGLU +
+unpermute, then the full backward (6 grouped GEMMs, unpermute/permute/top-k backward).
+
+`value` is grouped-GEMM TFLOP/s of the whole job (9 GEMMs per step, 2*T*K*d*H FLOPs each).
+Inputs (17.3 GB of weights) are far larger than L2, so no flush is needed between steps.
+Under torchrun (N > 1) every rank runs the same single-GPU layer on its own tokens
+(weak scaling); the expert-parallel path lives in moe_ops_b200.ep.
+
+`--impl reference` times the reference's PyTorch-native CPU path (restated in oracle/)
+on the host cores, on a bounded sample of the same workload (8 of the 64 experts with
+the same 256 rows per expert), and reports the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+CFG = dict(tokens=8192, d_model=4096, experts=64, top_k=2, hidden=11008)
+METRIC = "moe_layer_fwd_bwd_grouped_gemm_tflops"
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def _traffic_per_launch():
+    """DRAM bytes per grouped-GEMM launch from the committed ncu summary, if any."""
+    path = os.path.join(REPO, "profiles", "gmm_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.out, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        self.out.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax = float(parts[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _make_inputs(dev, T, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, CFG["d_model"], device=dev, generator=g).to(torch.bfloat16)
+    go = torch.randn(T, CFG["d_model"], device=dev, generator=g).to(torch.bfloat16)
+    return x, go
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from moe_ops_b200 import _lib
+    from moe_ops_b200.moe_layer import MoELayer, layer_gemm_flops
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        dist.init_process_group("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    T, d, E, K, H = CFG["tokens"], CFG["d_model"], CFG["experts"], CFG["top_k"], CFG["hidden"]
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layer = MoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16).init_normal(0.02, gen)
+    x, grad_out = _make_inputs(dev, T, 99 + rank)
+    flops_step = layer_gemm_flops(T, K, d, H)
+
+    def step(xin, gin):
+        for p in layer.parameters():
+            p.grad = None
+        xin = xin.detach().requires_grad_(True)
+        out = layer(xin)
+        out.backward(gin)
+        return out
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        step(x, grad_out)
+    barrier()
+
+    # ------------------------------------------------------------ device-timed region
+    sampler = ClockSampler(local)
+    sampler.start()
+    _lib.gemm_timing = []
+    launches0 = _lib.launch_count
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record()
+    for _ in range(args.steps):
+        step(x, grad_out)
+    ev1.record()
+    barrier()
+    clocks = sampler.stop()
+    ms_total = ev0.elapsed_time(ev1)
+    launches = _lib.launch_count - launches0
+    timing, _lib.gemm_timing = _lib.gemm_timing, None
+    gemm_ms = sum(a.elapsed_time(b) for _, a, b, _ in timing)
+    gemm_flops = sum(f for *_, f in timing)
+
+    # ------------------------------------------------------------ end to end (host buffers)
+    x_host = x.cpu().pin_memory()
+    g_host = grad_out.cpu().pin_memory()
+    res_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    g_dev = torch.empty_like(grad_out)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        g_dev.copy_(g_host, non_blocking=True)
+        out = step(x_dev, g_dev)
+        res_host.copy_(out.detach().float().sum().reshape(1), non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # max over ranks
+    t = torch.tensor([ms_total, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms = t.tolist()
+    ms_step = ms_total / args.steps
+    value = flops_step * world / (ms_step * 1e-3) / 1e12
+    e2e_value = flops_step * world / (e2e_ms / args.steps * 1e-3) / 1e12
+
+    peaks, peak_kind = _peaks()
+    achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    peak = peaks.get("bf16_tflops_sustained", 1400.0)
+    traffic = _traffic_per_launch()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
+        "config": {
+            "workload": "cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16",
+            "model": "moe_layer_swiglu", "global_batch": T * world, "seq_len": 1,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": "inputs larger than L2 (17.3 GB expert weights), no flush",
+            "gemm_flops_per_step": flops_step,
+        },
+        "roofline": {
+            "bound": "tensor",
+            "kernel": "gmm_sm100_kernel (grouped GEMM fwd/dgrad/wgrad, tcgen05)",
+            "achieved": round(achieved, 2) if achieved else None,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4) if achieved else None,
+            "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
+            "gemm_share_of_step": round(gemm_ms / ms_total, 4) if ms_total else None,
+            "traffic": traffic.get("bytes_per_launch") if traffic else None,
+        },
+        "e2e": {
+            "value": round(e2e_value, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(e2e_ms / args.steps, 4),
+            "h2d_bytes_per_step": x.numel() * 2 + grad_out.numel() * 2,
+            "d2h_bytes_per_step": 4,
+        },
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(steps=1, warmup=1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(steps: int = 1, warmup: int = 1, sample_experts: int = 8):
+    """The reference's PyTorch-native layer (oracle/moe_oracle.moe_layer_forward, the
+    per-expert loop of tests/test_moe.py:28-36) on the host cores, bf16, fwd + bwd, on a
+    sample: `sample_experts` experts with 256 rows each (T = 128 * sample_experts)."""
+    from oracle.moe_oracle import moe_layer_forward
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    d, K, H = CFG["d_model"], CFG["top_k"], CFG["hidden"]
+    E = sample_experts
+    T = 128 * E
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    go = torch.randn(T, d, generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, d, generator=g) * 0.02).to(torch.bfloat16).requires_grad_(True)
+    wg = (torch.randn(E, H, d, generator=g) * 0.02).to(torch.bfloat16).requires_grad_(True)
+    wu = (torch.randn(E, H, d, generator=g) * 0.02).to(torch.bfloat16).requires_grad_(True)
+    wd = (torch.randn(E, d, H, generator=g) * 0.02).to(torch.bfloat16).requires_grad_(True)
+
+    def step():
+        for p in (wr, wg, wu, wd):
+            p.grad = None
+        xi = x.detach().requires_grad_(True)
+        out = moe_layer_forward(xi, wr, wg, wu, wd, K, E)
+        out.backward(go)
+
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    sec = (time.perf_counter() - t0) / steps
+    flops = 9 * 2.0 * T * K * d * H
+    return {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "seconds_per_step": round(sec, 3),
+            "sample": f"{E} of 64 experts, T={T} tokens (256 rows/expert as in cfg4), "
+                      "d=4096 H=11008 top-2 bf16 fwd+bwd, torch CPU per-expert loop"}
+
+
+def run_reference(args):
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    base = cpu_baseline(steps=steps, warmup=1)
+    ms_step = base["seconds_per_step"] * 1e3
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": world,
+        "steps": steps, "warmup": 1, "ms_per_step": round(ms_step, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded)", "impl": "reference",
+        "config": {"workload": "cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16",
+                   "model": "moe_layer_swiglu", "sample": base["sample"]},
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

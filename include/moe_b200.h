@@ -1,0 +1,131 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) MoE operator library.
+ *
+ * Every entry point:
+ *   - takes device pointers the caller allocated (outputs and workspace included);
+ *   - enqueues its kernels on the given CUDA stream (`stream` is a cudaStream_t,
+ *     NULL = legacy default stream) and never synchronises the host;
+ *   - returns 0 on success or a positive MOE_ERR_* code; the message for the last
+ *     failure on the calling thread is available from moe_last_error_string().
+ * No C++ exceptions and no torch types cross this boundary.
+ *
+ * Tensor layouts are row-major and contiguous.  `dtype` codes: MOE_F32, MOE_F16, MOE_BF16.
+ * Offsets follow the reference's grouped-GEMM contract: `num_offsets` is E+1
+ * (offsets[0] = 0, offsets[e+1] = end row of expert e) or E (offsets[e] = end row).
+ *
+ * Each declaration cites the reference interface (echogujy/moe_ops, package
+ * triton_gmm_ops) that it replaces.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum moe_dtype { MOE_F32 = 0, MOE_F16 = 1, MOE_BF16 = 2 };
+
+enum moe_status {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = 1,   /* bad shape / dtype / pointer combination          */
+  MOE_ERR_UNSUPPORTED = 2,   /* valid request this build does not implement      */
+  MOE_ERR_CUDA = 3,          /* a CUDA runtime call or kernel launch failed       */
+  MOE_ERR_WORKSPACE = 4,     /* workspace missing or smaller than required        */
+  MOE_ERR_DEVICE = 5         /* a kernel reported a device-side error flag        */
+};
+
+/* Library version string, e.g. "moe_b200 0.1.0 sm_100a". */
+const char* moe_version(void);
+
+/* Message describing the last non-zero status returned on this host thread. */
+const char* moe_last_error_string(void);
+
+/* Reads and clears the library's device-side error word on the current device
+ * (synchronises the device).  0 = no error; 1 = a bounded wait inside a GEMM
+ * kernel gave up; 2 = an expert index outside [0, E) was seen by permute. */
+int moe_read_device_error(int* code_out);
+
+/* ---------------------------------------------------------------- top-k softmax
+ * Replaces tg::fused_topk_softmax_fwd
+ * (triton_gmm_ops/fused_topk_softmax_ops.py:121-138, kernel :17-70).
+ * logits [T, E] (dtype), weights [T, K] (same dtype), indices [T, K] int32.
+ * Top-K by value with ties broken towards the lower expert index, then a softmax
+ * over the K selected values computed in fp32. */
+int moe_topk_softmax_fwd(const void* logits, int dtype, int64_t num_tokens, int32_t num_experts,
+                         int32_t topk, void* weights, int32_t* indices, void* stream);
+
+/* Replaces tg::fused_topk_softmax_bwd (fused_topk_softmax_ops.py:150-165, kernel :83-114).
+ * grad_logits [T, E] is fully written: w*(g - sum_k g*w) at the selected experts, 0 elsewhere. */
+int moe_topk_softmax_bwd(const void* grad_weights, const void* weights, const int32_t* indices,
+                         int dtype, int64_t num_tokens, int32_t num_experts, int32_t topk,
+                         void* grad_logits, void* stream);
+
+/* ---------------------------------------------------------------- permute
+ * Bytes of device workspace moe_permute needs for these sizes. */
+size_t moe_permute_workspace_bytes(int64_t num_tokens, int32_t topk, int32_t num_experts);
+
+/* Replaces tg::permute_countsort (triton_gmm_ops/permute_ops.py:82-110) together with
+ * _group_offsets (:36-43).  input [T, C] (dtype), indices [T, K] int32 expert ids.
+ * Writes offsets [E+1] (offsets[0]=0, inclusive prefix of the expert histogram),
+ * row_id_map [K*T] (row_id_map[k*T + t] = destination row of slot (t,k)) and
+ * permuted [num_out, C] with permuted[row_id_map[k*T+t]] = input[t].  Rows are
+ * grouped by expert in stable slot order (the order of a stable argsort of the
+ * flattened indices).  num_out >= T*K; rows past T*K are left unwritten. */
+int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                int32_t topk, int64_t num_cols, int32_t num_experts, int64_t num_out,
+                void* permuted, int32_t* row_id_map, int32_t* offsets, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- unpermute
+ * Replaces tg::unpermute_forward (triton_gmm_ops/unpermute_ops.py:58-72, kernel :20-55).
+ * out[t] = sum_k prob[t,k] * input[row_id_map[k*T+t]], accumulated in fp32 in k order
+ * (product rounded, then sum rounded), cast to dtype.  prob [T, K] of prob_dtype.
+ * A NULL prob means prob == 1 everywhere: this is permute_backward
+ * (triton_gmm_ops/permute_ops.py:130-133). */
+int moe_unpermute_fwd(const void* input, int dtype, const int32_t* row_id_map, const void* prob,
+                      int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols, void* out,
+                      void* stream);
+
+/* Replaces tg::unpermute_backward (unpermute_ops.py:153-172, kernel :93-150).
+ * act_grad[row_id_map[k*T+t]] = cast(prob[t,k] * grad_out[t]) and
+ * prob_grad[t,k] = sum_c grad_out[t,c] * input_fwd[row_id_map[k*T+t], c] (fp32, cast to
+ * prob_dtype).  Rows of act_grad that row_id_map does not name are left unwritten. */
+int moe_unpermute_bwd(const void* grad_out, const void* input_fwd, int dtype,
+                      const int32_t* row_id_map, const void* prob, int prob_dtype,
+                      int64_t num_tokens, int32_t topk, int64_t num_cols, void* act_grad,
+                      void* prob_grad, void* stream);
+
+/* ---------------------------------------------------------------- grouped GEMM
+ * Replaces tg::gmm_tma_fwd_raw / group_gemm_tma_fn
+ * (triton_gmm_ops/grouped_gemm_ops_sm90.py:151-202) and tg::gmm_fwd_raw
+ * (triton_gmm_ops/grouped_gemm_ops.py:75-101).
+ * A [M_total, K]; B [E, N, K] if trans_b else [E, K, N]; C [M_total, N].
+ * C[rows of e] = A[rows of e] @ (B[e]^T if trans_b else B[e]), fp32 accumulation.
+ * bf16/fp16 run on the tcgen05 tensor-core kernel; fp32 (and shapes whose rows are not
+ * 16-byte multiples) on a CUDA-core kernel with fp32 FMA. */
+int moe_gmm_fwd(const void* A, const void* B, void* C, const int32_t* offsets,
+                int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t num_experts,
+                int trans_b, int dtype, void* stream);
+
+/* dgrad of moe_gmm_fwd, the grad_A branch of GroupedGEMMAutogradSM90.backward
+ * (grouped_gemm_ops_sm90.py:224-233).  grad_C [M_total, N] -> grad_A [M_total, K].
+ * Reads B in place for both values of trans_b (no transposed weight copy). */
+int moe_gmm_dgrad(const void* grad_C, const void* B, void* grad_A, const int32_t* offsets,
+                  int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
+                  int32_t num_experts, int trans_b, int dtype, void* stream);
+
+/* wgrad of moe_gmm_fwd: replaces tg::gmm_bwd_B_raw (grouped_gemm_ops.py:174-192).
+ * grad_B [E, N, K] if trans_b else [E, K, N] (the reference supports trans_b only);
+ * experts with no rows get zeros. */
+int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t* offsets,
+                  int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
+                  int32_t num_experts, int trans_b, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

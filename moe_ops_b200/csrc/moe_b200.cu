@@ -1,0 +1,489 @@
+// C ABI of the B200 MoE operator library (declarations and contracts: include/moe_b200.h).
+// The library is one translation unit: this file includes every kernel header.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "common.cuh"
+#include "gmm_simt.cuh"
+#include "gmm_sm100.cuh"
+#include "permute.cuh"
+#include "topk_softmax.cuh"
+
+namespace moe {
+
+static thread_local char t_err_msg[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_err_msg, sizeof(t_err_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int num_sms(int device) {
+  static int cache[64] = {0};
+  if (device >= 0 && device < 64 && cache[device] > 0) return cache[device];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+    n = 148;
+  if (device >= 0 && device < 64) cache[device] = n;
+  return n;
+}
+
+static int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+// ---------------------------------------------------------------- tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 16-bit element tensor map with 128-byte swizzle; dims/box innermost first.
+static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint64_t* dims,
+                    const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t gdim[3], gstride[2];
+  cuuint32_t bdim[3], estr[3] = {1, 1, 1};
+  uint64_t stride = 2;
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    if (i > 0) gstride[i - 1] = stride;
+    stride *= dims[i];
+  }
+  const CUtensorMapDataType dt =
+      dtype == MOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rank=%d dims=%llu,%llu,%llu",
+                     (int)r, rank, (unsigned long long)dims[0],
+                     (unsigned long long)(rank > 1 ? dims[1] : 0),
+                     (unsigned long long)(rank > 2 ? dims[2] : 0));
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------- GEMM launchers
+template <int MODE, int FMT, bool A_MN, bool B_MN, typename OutT>
+static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const gmm::Params& p,
+                        cudaStream_t stream) {
+  auto kern = gmm::gmm_sm100_kernel<MODE, FMT, A_MN, B_MN, OutT>;
+  const int dev = current_device();
+  static unsigned long long attr_set = 0;  // per-device bitmask
+  if (dev < 64 && !(attr_set & (1ull << dev))) {
+    MOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)gmm::kSmemBytes));
+    attr_set |= 1ull << dev;
+  }
+  kern<<<num_sms(dev), gmm::kThreads, gmm::kSmemBytes, stream>>>(ma, mb, p);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Row mode (forward / dgrad): C[m_total, n_out] = A[m_total, k_red] . op(B[g]).
+// b_mn: B[g] stored [k_red, n_out] (MN-major) instead of [n_out, k_red].
+static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offsets, int plus_one,
+                    int64_t m_total, int64_t n_out, int64_t k_red, int E, bool b_mn, int dtype,
+                    cudaStream_t stream) {
+  if (m_total == 0 || n_out == 0) return MOE_OK;
+  const bool tc = dtype != MOE_F32 && k_red % 8 == 0 && n_out % 8 == 0 && E <= gmm::kMaxGroups &&
+                  aligned16(A) && aligned16(B) && aligned16(C) && m_total < (1ll << 31) &&
+                  n_out < (1ll << 31) && k_red < (1ll << 31);
+  if (!tc || k_red == 0) {
+    if (k_red == 0) {
+      MOE_CUDA_CHECK(cudaMemsetAsync(C, 0, (size_t)m_total * n_out * dtype_size(dtype), stream));
+      return MOE_OK;
+    }
+    const dim3 grid((unsigned)((m_total + simt::TM - 1) / simt::TM),
+                    (unsigned)((n_out + simt::TN - 1) / simt::TN), (unsigned)E);
+    MOE_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "gmm: grid too large for the CUDA-core path");
+    switch (dtype) {
+      case MOE_F32:
+        simt::gmm_rows_simt_kernel<float><<<grid, 256, 0, stream>>>(
+            (const float*)A, (const float*)B, (float*)C, offsets, plus_one, n_out, k_red, b_mn);
+        break;
+      case MOE_F16:
+        simt::gmm_rows_simt_kernel<__half><<<grid, 256, 0, stream>>>(
+            (const __half*)A, (const __half*)B, (__half*)C, offsets, plus_one, n_out, k_red, b_mn);
+        break;
+      default:
+        simt::gmm_rows_simt_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+            (const __nv_bfloat16*)A, (const __nv_bfloat16*)B, (__nv_bfloat16*)C, offsets,
+            plus_one, n_out, k_red, b_mn);
+    }
+    MOE_LAUNCH_CHECK();
+    return MOE_OK;
+  }
+  CUtensorMap ma, mb;
+  {
+    const uint64_t dims[2] = {(uint64_t)k_red, (uint64_t)m_total};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, (uint32_t)gmm::BM};
+    int rc = make_map(&ma, A, dtype, 2, dims, box);
+    if (rc) return rc;
+  }
+  if (!b_mn) {
+    const uint64_t dims[3] = {(uint64_t)k_red, (uint64_t)n_out, (uint64_t)E};
+    const uint32_t box[3] = {(uint32_t)gmm::BK, (uint32_t)gmm::BN, 1};
+    int rc = make_map(&mb, B, dtype, 3, dims, box);
+    if (rc) return rc;
+  } else {
+    const uint64_t dims[3] = {(uint64_t)n_out, (uint64_t)k_red, (uint64_t)E};
+    const uint32_t box[3] = {64, (uint32_t)gmm::BK, 1};
+    int rc = make_map(&mb, B, dtype, 3, dims, box);
+    if (rc) return rc;
+  }
+  gmm::Params p;
+  p.offsets = offsets;
+  p.offsets_plus_one = plus_one;
+  p.num_groups = E;
+  p.m_total = m_total;
+  p.n_out = (int)n_out;
+  p.p_out = 0;
+  p.k_red = (int)k_red;
+  p.out = C;
+  if (dtype == MOE_BF16) {
+    return b_mn ? launch_sm100<gmm::kModeRows, 1, false, true, __nv_bfloat16>(ma, mb, p, stream)
+                : launch_sm100<gmm::kModeRows, 1, false, false, __nv_bfloat16>(ma, mb, p, stream);
+  }
+  return b_mn ? launch_sm100<gmm::kModeRows, 0, false, true, __half>(ma, mb, p, stream)
+              : launch_sm100<gmm::kModeRows, 0, false, false, __half>(ma, mb, p, stream);
+}
+
+// Wgrad mode: Out[g] [P, Q] = X[rows of g]^T . Y[rows of g]; X [m_total, P], Y [m_total, Q].
+static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* offsets, int plus_one,
+                     int64_t m_total, int64_t P, int64_t Q, int E, int dtype, cudaStream_t stream) {
+  if (P == 0 || Q == 0 || E == 0) return MOE_OK;
+  const bool tc = dtype != MOE_F32 && P % 8 == 0 && Q % 8 == 0 && E <= gmm::kMaxGroups &&
+                  aligned16(X) && aligned16(Y) && aligned16(Out) && m_total > 0 &&
+                  m_total < (1ll << 31) && P < (1ll << 31) && Q < (1ll << 31);
+  if (!tc) {
+    const dim3 grid((unsigned)((Q + simt::TN - 1) / simt::TN), (unsigned)((P + simt::TM - 1) / simt::TM),
+                    (unsigned)E);
+    MOE_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "gmm wgrad: grid too large for the CUDA-core path");
+    switch (dtype) {
+      case MOE_F32:
+        simt::gmm_wgrad_simt_kernel<float><<<grid, 256, 0, stream>>>(
+            (const float*)X, (const float*)Y, (float*)Out, offsets, plus_one, P, Q);
+        break;
+      case MOE_F16:
+        simt::gmm_wgrad_simt_kernel<__half><<<grid, 256, 0, stream>>>(
+            (const __half*)X, (const __half*)Y, (__half*)Out, offsets, plus_one, P, Q);
+        break;
+      default:
+        simt::gmm_wgrad_simt_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+            (const __nv_bfloat16*)X, (const __nv_bfloat16*)Y, (__nv_bfloat16*)Out, offsets,
+            plus_one, P, Q);
+    }
+    MOE_LAUNCH_CHECK();
+    return MOE_OK;
+  }
+  CUtensorMap mx, my;
+  {
+    const uint64_t dims[2] = {(uint64_t)P, (uint64_t)m_total};
+    const uint32_t box[2] = {64, (uint32_t)gmm::BK};
+    int rc = make_map(&mx, X, dtype, 2, dims, box);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)Q, (uint64_t)m_total};
+    const uint32_t box[2] = {64, (uint32_t)gmm::BK};
+    int rc = make_map(&my, Y, dtype, 2, dims, box);
+    if (rc) return rc;
+  }
+  gmm::Params p;
+  p.offsets = offsets;
+  p.offsets_plus_one = plus_one;
+  p.num_groups = E;
+  p.m_total = m_total;
+  p.n_out = (int)Q;
+  p.p_out = (int)P;
+  p.k_red = 0;
+  p.out = Out;
+  if (dtype == MOE_BF16)
+    return launch_sm100<gmm::kModeWgrad, 1, true, true, __nv_bfloat16>(mx, my, p, stream);
+  return launch_sm100<gmm::kModeWgrad, 0, true, true, __half>(mx, my, p, stream);
+}
+
+static int check_gmm_args(const void* a, const void* b, const void* c, const int32_t* offsets,
+                          int num_offsets, int64_t m_total, int64_t n, int64_t k, int E, int dtype) {
+  MOE_REQUIRE(dtype_ok(dtype), "gmm: bad dtype %d", dtype);
+  MOE_REQUIRE(E >= 0 && m_total >= 0 && n >= 0 && k >= 0, "gmm: negative size");
+  MOE_REQUIRE(num_offsets == E || num_offsets == E + 1,
+              "gmm: num_offsets must be E or E+1 (got %d, E=%d)", num_offsets, E);
+  MOE_REQUIRE(E == 0 || offsets != nullptr, "gmm: offsets is NULL");
+  MOE_REQUIRE((a && b && c) || m_total == 0 || E == 0, "gmm: NULL operand");
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------- permute workspace
+struct PermuteWorkspace {
+  int64_t num_tiles;
+  size_t cnt_bytes;
+};
+static PermuteWorkspace permute_ws(int64_t T, int K, int E) {
+  PermuteWorkspace w;
+  w.num_tiles = permute_num_tiles(T * (int64_t)K);
+  w.cnt_bytes = (size_t)w.num_tiles * E * sizeof(int32_t);
+  return w;
+}
+
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+const char* moe_version(void) { return "moe_b200 0.1.0 sm_100a"; }
+
+const char* moe_last_error_string(void) { return t_err_msg; }
+
+int moe_read_device_error(int* code_out) {
+  int v = 0, zero = 0;
+  MOE_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
+  MOE_CUDA_CHECK(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
+  if (code_out) *code_out = v;
+  return MOE_OK;
+}
+
+int moe_topk_softmax_fwd(const void* logits, int dtype, int64_t num_tokens, int32_t E, int32_t K,
+                         void* weights, int32_t* indices, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "topk_softmax: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && E > 0 && K > 0 && K <= E && K <= 32,
+              "topk_softmax: need 0 < K <= min(E, 32) (E=%d, K=%d)", E, K);
+  if (num_tokens == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (dtype) {
+    case MOE_F32: return launch_topk_fwd<float>(logits, num_tokens, E, K, weights, indices, s);
+    case MOE_F16: return launch_topk_fwd<__half>(logits, num_tokens, E, K, weights, indices, s);
+    default: return launch_topk_fwd<__nv_bfloat16>(logits, num_tokens, E, K, weights, indices, s);
+  }
+}
+
+int moe_topk_softmax_bwd(const void* grad_weights, const void* weights, const int32_t* indices,
+                         int dtype, int64_t num_tokens, int32_t E, int32_t K, void* grad_logits,
+                         void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "topk_softmax_bwd: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && E > 0 && K > 0 && K <= 32, "topk_softmax_bwd: bad E=%d K=%d", E, K);
+  if (num_tokens == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (dtype) {
+    case MOE_F32: return launch_topk_bwd<float>(grad_weights, weights, indices, num_tokens, E, K, grad_logits, s);
+    case MOE_F16: return launch_topk_bwd<__half>(grad_weights, weights, indices, num_tokens, E, K, grad_logits, s);
+    default: return launch_topk_bwd<__nv_bfloat16>(grad_weights, weights, indices, num_tokens, E, K, grad_logits, s);
+  }
+}
+
+size_t moe_permute_workspace_bytes(int64_t num_tokens, int32_t topk, int32_t E) {
+  if (num_tokens <= 0 || topk <= 0 || E <= 0) return 16;
+  return permute_ws(num_tokens, topk, E).cnt_bytes + 16;
+}
+
+int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                int32_t topk, int64_t num_cols, int32_t E, int64_t num_out, void* permuted,
+                int32_t* row_id_map, int32_t* offsets, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "permute: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0,
+              "permute: bad sizes T=%lld K=%d C=%lld", (long long)num_tokens, topk, (long long)num_cols);
+  MOE_REQUIRE(E > 0 && E <= kMaxExperts, "permute: need 0 < E <= %d (E=%d)", kMaxExperts, E);
+  const int64_t num_slots = num_tokens * topk;
+  MOE_REQUIRE(num_out >= num_slots, "permute: num_out (%lld) < T*K (%lld)", (long long)num_out,
+              (long long)num_slots);
+  MOE_REQUIRE(num_slots < (1ll << 31), "permute: T*K must fit in int32");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (num_slots == 0) {
+    MOE_CUDA_CHECK(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), s));
+    return MOE_OK;
+  }
+  const PermuteWorkspace w = permute_ws(num_tokens, topk, E);
+  if (workspace == nullptr || workspace_bytes < w.cnt_bytes)
+    return set_error(MOE_ERR_WORKSPACE, "permute: workspace needs %zu bytes (got %zu)", w.cnt_bytes,
+                     workspace_bytes);
+  int32_t* cnt = static_cast<int32_t*>(workspace);
+  const unsigned tiles = (unsigned)w.num_tiles;
+  permute_hist_kernel<<<tiles, kPermTile, E * sizeof(int32_t), s>>>(indices, num_slots, E, cnt,
+                                                                     w.num_tiles);
+  MOE_LAUNCH_CHECK();
+  permute_scan_kernel<<<1, kScanThreads, 0, s>>>(cnt, w.num_tiles, E, offsets);
+  MOE_LAUNCH_CHECK();
+  const size_t rank_smem = (size_t)kPermTileWarps * E * sizeof(int32_t);
+  if (rank_smem > 48 * 1024) {
+    MOE_CUDA_CHECK(cudaFuncSetAttribute(permute_rank_kernel,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rank_smem));
+  }
+  permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
+                                                          cnt, w.num_tiles, row_id_map);
+  MOE_LAUNCH_CHECK();
+  if (num_cols == 0) return MOE_OK;
+  const int es = dtype_size(dtype);
+  const bool vec = (num_cols * es) % 16 == 0 && aligned16(input) && aligned16(permuted);
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+#define MOE_COPY(TT)                                                                                 \
+  if (vec)                                                                                          \
+    permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>(                                   \
+        (const TT*)input, row_id_map, (TT*)permuted, num_tokens, topk, num_cols);                  \
+  else                                                                                              \
+    permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>(                                  \
+        (const TT*)input, row_id_map, (TT*)permuted, num_tokens, topk, num_cols);
+  switch (dtype) {
+    case MOE_F32: MOE_COPY(float) break;
+    case MOE_F16: MOE_COPY(__half) break;
+    default: MOE_COPY(__nv_bfloat16) break;
+  }
+#undef MOE_COPY
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_unpermute_fwd(const void* input, int dtype, const int32_t* row_id_map, const void* prob,
+                      int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols, void* out,
+                      void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype) && (prob == nullptr || dtype_ok(prob_dtype)),
+              "unpermute: bad dtype %d / prob dtype %d", dtype, prob_dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "unpermute: bad sizes");
+  if (num_tokens == 0 || num_cols == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int es = dtype_size(dtype);
+  const bool vec = (num_cols * es) % 16 == 0 && aligned16(input) && aligned16(out);
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+  const int pd = prob == nullptr ? MOE_F32 : prob_dtype;
+#define MOE_UNP(TT, PP)                                                                              \
+  if (vec)                                                                                          \
+    unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                              \
+        (const TT*)input, row_id_map, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);      \
+  else                                                                                              \
+    unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                             \
+        (const TT*)input, row_id_map, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);
+#define MOE_UNP_P(TT)                                                                                \
+  switch (pd) {                                                                                     \
+    case MOE_F32: MOE_UNP(TT, float) break;                                                         \
+    case MOE_F16: MOE_UNP(TT, __half) break;                                                        \
+    default: MOE_UNP(TT, __nv_bfloat16) break;                                                      \
+  }
+  switch (dtype) {
+    case MOE_F32: MOE_UNP_P(float) break;
+    case MOE_F16: MOE_UNP_P(__half) break;
+    default: MOE_UNP_P(__nv_bfloat16) break;
+  }
+#undef MOE_UNP_P
+#undef MOE_UNP
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_unpermute_bwd(const void* grad_out, const void* input_fwd, int dtype,
+                      const int32_t* row_id_map, const void* prob, int prob_dtype,
+                      int64_t num_tokens, int32_t topk, int64_t num_cols, void* act_grad,
+                      void* prob_grad, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype) && dtype_ok(prob_dtype), "unpermute_bwd: bad dtype");
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "unpermute_bwd: bad sizes");
+  MOE_REQUIRE(prob != nullptr && prob_grad != nullptr, "unpermute_bwd: prob / prob_grad is NULL");
+  if (num_tokens == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int es = dtype_size(dtype);
+  const bool vec = (num_cols * es) % 16 == 0 && aligned16(grad_out) && aligned16(input_fwd) &&
+                   aligned16(act_grad);
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+#define MOE_UB(TT, PP, KM)                                                                           \
+  if (vec)                                                                                          \
+    unpermute_bwd_kernel<TT, PP, KM, true><<<grid, kRowWarps * 32, 0, s>>>(                          \
+        (const TT*)grad_out, (const TT*)input_fwd, row_id_map, (const PP*)prob, (TT*)act_grad,     \
+        (PP*)prob_grad, num_tokens, topk, num_cols);                                               \
+  else                                                                                              \
+    unpermute_bwd_kernel<TT, PP, KM, false><<<grid, kRowWarps * 32, 0, s>>>(                         \
+        (const TT*)grad_out, (const TT*)input_fwd, row_id_map, (const PP*)prob, (TT*)act_grad,     \
+        (PP*)prob_grad, num_tokens, topk, num_cols);
+#define MOE_UB_K(TT, PP)                                                                             \
+  if (topk <= 2) { MOE_UB(TT, PP, 2) }                                                              \
+  else if (topk <= 4) { MOE_UB(TT, PP, 4) }                                                         \
+  else if (topk <= 8) { MOE_UB(TT, PP, 8) }                                                         \
+  else if (topk <= 16) { MOE_UB(TT, PP, 16) }                                                       \
+  else { MOE_UB(TT, PP, 32) }
+#define MOE_UB_P(TT)                                                                                 \
+  switch (prob_dtype) {                                                                             \
+    case MOE_F32: MOE_UB_K(TT, float) break;                                                        \
+    case MOE_F16: MOE_UB_K(TT, __half) break;                                                       \
+    default: MOE_UB_K(TT, __nv_bfloat16) break;                                                     \
+  }
+  switch (dtype) {
+    case MOE_F32: MOE_UB_P(float) break;
+    case MOE_F16: MOE_UB_P(__half) break;
+    default: MOE_UB_P(__nv_bfloat16) break;
+  }
+#undef MOE_UB_P
+#undef MOE_UB_K
+#undef MOE_UB
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_gmm_fwd(const void* A, const void* B, void* C, const int32_t* offsets, int32_t num_offsets,
+                int64_t m_total, int64_t n, int64_t k, int32_t E, int trans_b, int dtype,
+                void* stream) {
+  int rc = check_gmm_args(A, B, C, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  if (E == 0) return MOE_OK;
+  // trans_b: B[e] is [N, K] (K-major operand); else [K, N] (MN-major operand).
+  return gmm_rows(A, B, C, offsets, num_offsets == E + 1, m_total, n, k, E, !trans_b, dtype,
+                  (cudaStream_t)stream);
+}
+
+int moe_gmm_dgrad(const void* grad_C, const void* B, void* grad_A, const int32_t* offsets,
+                  int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t E,
+                  int trans_b, int dtype, void* stream) {
+  int rc = check_gmm_args(grad_C, B, grad_A, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  if (E == 0) return MOE_OK;
+  // grad_A [M, K] = grad_C [M, N] . B'[e], contraction over N.  With trans_b, B[e] is
+  // [N, K]: contraction rows, output columns contiguous -> MN-major operand.  Without,
+  // B[e] is [K, N]: contraction contiguous -> K-major operand.
+  return gmm_rows(grad_C, B, grad_A, offsets, num_offsets == E + 1, m_total, k, n, E, trans_b != 0,
+                  dtype, (cudaStream_t)stream);
+}
+
+int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t* offsets,
+                  int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t E,
+                  int trans_b, int dtype, void* stream) {
+  int rc = check_gmm_args(A, grad_C, grad_B, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  if (E == 0) return MOE_OK;
+  const int plus_one = num_offsets == E + 1;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (m_total == 0) {
+    MOE_CUDA_CHECK(cudaMemsetAsync(grad_B, 0, (size_t)E * n * k * dtype_size(dtype), s));
+    return MOE_OK;
+  }
+  // trans_b: grad_B[e] [N, K] = grad_C_e^T A_e;  else grad_B[e] [K, N] = A_e^T grad_C_e.
+  if (trans_b) return gmm_wgrad(grad_C, A, grad_B, offsets, plus_one, m_total, n, k, E, dtype, s);
+  return gmm_wgrad(A, grad_C, grad_B, offsets, plus_one, m_total, k, n, E, dtype, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,72 @@
+"""SwiGLU MoE layer assembled from the library's ops (single GPU).
+
+Same structure as the reference's example layer SingleGpuMoE (tests/test_moe.py:49-87):
+
+    logits  = x @ w_router^T                          (torch GEMM, [T, E])
+    w, idx  = fused_topk_softmax(logits, K)
+    perm, row_id_map, offsets = permute(x, idx, E=E)
+    gate    = grouped_gemm(perm, w_gate, offsets)     [T*K, H]
+    up      = grouped_gemm(perm, w_up, offsets)       [T*K, H]
+    h       = silu(gate) * up                         (torch elementwise)
+    down    = grouped_gemm(h, w_down, offsets)        [T*K, d]
+    out     = unpermute(down, row_id_map, w, T, K)
+
+Weights: w_router [E, d], w_gate / w_up [E, H, d], w_down [E, d, H] (trans_b=True layout).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .fused_topk_softmax_ops import fused_topk_softmax
+from .grouped_gemm_ops import grouped_gemm
+from .permute_ops import permute
+from .unpermute_ops import unpermute
+
+
+def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Tensor,
+                      w_up: torch.Tensor, w_down: torch.Tensor, top_k: int,
+                      fp32_routing: bool = False) -> torch.Tensor:
+    E = w_gate.shape[0]
+    num_tokens = x.shape[0]
+    logits = x @ w_router.t()
+    weights, indices = fused_topk_softmax(logits, top_k, fp32_routing=fp32_routing)
+    permuted, row_id_map, offsets = permute(x, indices, E=E)
+    gate = grouped_gemm(permuted, w_gate, offsets, trans_b=True)
+    up = grouped_gemm(permuted, w_up, offsets, trans_b=True)
+    h = F.silu(gate) * up
+    down = grouped_gemm(h, w_down, offsets, trans_b=True)
+    return unpermute(down, row_id_map, weights, num_tokens, top_k)
+
+
+class MoELayer(torch.nn.Module):
+    """Single-GPU SwiGLU MoE layer (parameters as in the reference's SingleGpuMoE)."""
+
+    def __init__(self, d_model: int, num_experts: int, top_k: int, hidden: int,
+                 fp32_routing: bool = False, device=None, dtype=None):
+        super().__init__()
+        kw = dict(device=device, dtype=dtype)
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.fp32_routing = fp32_routing
+        self.w_router = torch.nn.Parameter(torch.empty(num_experts, d_model, **kw))
+        self.w_gate = torch.nn.Parameter(torch.empty(num_experts, hidden, d_model, **kw))
+        self.w_up = torch.nn.Parameter(torch.empty(num_experts, hidden, d_model, **kw))
+        self.w_down = torch.nn.Parameter(torch.empty(num_experts, d_model, hidden, **kw))
+
+    @torch.no_grad()
+    def init_normal(self, std: float = 0.02, generator=None) -> "MoELayer":
+        for p in self.parameters():
+            p.normal_(0.0, std, generator=generator)
+        return self
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return moe_layer_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down,
+                                 self.top_k, self.fp32_routing)
+
+
+def layer_gemm_flops(num_tokens: int, top_k: int, d_model: int, hidden: int,
+                     backward: bool = True) -> float:
+    """Grouped-GEMM FLOPs of one layer step: 3 GEMMs forward (+ 6 backward)."""
+    per_gemm = 2.0 * num_tokens * top_k * d_model * hidden
+    return per_gemm * (9 if backward else 3)

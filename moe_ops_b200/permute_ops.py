@@ -1,0 +1,103 @@
+"""Counting-sort permute and its backward.
+
+Drop-in for the reference's permute API (triton_gmm_ops/permute_ops.py:82-159):
+
+    permute(input, indices, num_out_tokens=0, E=None) -> (permuted, row_id_map, offsets)
+    permute_backward(grad_permuted, row_id_map, num_tokens, topK) -> grad_input
+
+``offsets`` is int32 [E+1] with offsets[0] = 0 and offsets[e+1] the end row of expert e,
+exactly what grouped_gemm consumes.  ``row_id_map[k*T + t]`` is the row of ``permuted``
+holding token t's k-th slot.  Unlike the reference's atomic scatter, rows inside an
+expert group come out in slot order (stable), so results are deterministic.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .unpermute_ops import _unpermute_call
+
+_NS = "moeb200"
+
+
+@torch.library.custom_op(f"{_NS}::permute_countsort", mutates_args=())
+def permute_countsort(input: torch.Tensor, indices: torch.Tensor, num_out_tokens: int = 0,
+                      E: int = 0) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    _lib.require_cuda(input, indices)
+    input = input.contiguous()
+    if indices.dim() == 1:
+        indices = indices.unsqueeze(1)
+    num_tokens, num_cols = input.shape
+    topK = indices.shape[1]
+    flat = indices.reshape(-1)
+    if flat.dtype != torch.int32:
+        flat = flat.to(torch.int32)
+    flat = flat.contiguous()
+    num_total = num_tokens * topK
+    num_out = num_out_tokens if num_out_tokens > 0 else num_total
+    # offsets always sum to num_total, so permuted holds at least that many rows
+    # (capacity dropping is not part of the reference contract either).
+    num_out = max(num_out, num_total)
+    if E <= 0:
+        E = int(flat.max()) + 1 if num_total > 0 else 1
+    lib = _lib.load()
+    permuted = torch.empty(num_out, num_cols, device=input.device, dtype=input.dtype)
+    row_id_map = torch.empty(num_total, dtype=torch.int32, device=input.device)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=input.device)
+    ws_bytes = lib.moe_permute_workspace_bytes(num_tokens, topK, E)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
+    with torch.cuda.device(input.device):
+        st = lib.moe_permute(
+            _lib.ptr(input), _lib.dtype_code(input.dtype), _lib.ptr(flat), num_tokens, topK,
+            num_cols, E, num_out, _lib.ptr(permuted), _lib.ptr(row_id_map), _lib.ptr(offsets),
+            _lib.ptr(ws), ws_bytes, _lib.stream_of(input))
+    _lib.check(st, "moe_permute")
+    _lib.count_launches(4)
+    return permuted, row_id_map, offsets
+
+
+@permute_countsort.register_fake
+def _(input, indices, num_out_tokens=0, E=0):
+    num_tokens, num_cols = input.shape
+    topK = indices.shape[1] if indices.dim() > 1 else 1
+    num_total = num_tokens * topK
+    num_out = max(num_out_tokens, num_total)
+    off_len = E + 1 if E > 0 else num_total + 1
+    return (torch.empty(num_out, num_cols, device=input.device, dtype=input.dtype),
+            torch.empty(num_total, device=input.device, dtype=torch.int32),
+            torch.empty(off_len, device=input.device, dtype=torch.int32))
+
+
+def permute_backward(grad_permuted: torch.Tensor, row_id_map: torch.Tensor,
+                     num_tokens: int, topK: int) -> torch.Tensor:
+    """grad_input[t] = sum_k grad_permuted[row_id_map[k*T+t]] (fp32 accumulation).
+
+    Same as unpermute with prob = 1 (permute_ops.py:130-133); no ones tensor is built.
+    """
+    return _unpermute_call(grad_permuted, row_id_map, None, num_tokens, topK)
+
+
+class PermuteAutograd(torch.autograd.Function):
+    """Same contract as the reference's PermuteAutograd (permute_ops.py:136-154)."""
+
+    @staticmethod
+    def forward(ctx, input, indices, num_out_tokens=0, E=None):
+        ctx.num_tokens = input.shape[0]
+        ctx.topK = indices.shape[1] if indices.ndim > 1 else 1
+        e = E if E is not None else 0
+        permuted, row_id_map, offsets = torch.ops.moeb200.permute_countsort(
+            input, indices, num_out_tokens, e)
+        ctx.save_for_backward(row_id_map)
+        ctx.mark_non_differentiable(row_id_map, offsets)
+        return permuted, row_id_map, offsets
+
+    @staticmethod
+    def backward(ctx, grad_permuted, grad_row_id_map, grad_offsets):
+        (row_id_map,) = ctx.saved_tensors
+        grad_input = permute_backward(grad_permuted, row_id_map, ctx.num_tokens, ctx.topK)
+        return grad_input, None, None, None
+
+
+def permute(input, indices, num_out_tokens=0, E=None):
+    """Differentiable counting-sort permute."""
+    return PermuteAutograd.apply(input, indices, num_out_tokens, E)
