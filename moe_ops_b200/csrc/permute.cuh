@@ -194,11 +194,14 @@ permute_copy_kernel(const T* __restrict__ input, const int32_t* __restrict__ row
       }
     }
   } else {
-    for (int64_t c = lane; c < num_cols; c += 32) {
-      const T v = src[c];
+    // Warp-uniform loop: every lane takes part in the shuffles.
+    for (int64_t c0 = 0; c0 < num_cols; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const bool in = c < num_cols;
+      const T v = in ? src[c] : T();
       for (int k = 0; k < K; ++k) {
         const int32_t d = __shfl_sync(0xffffffffu, dst_lane, k);
-        if (d >= 0) permuted[(int64_t)d * num_cols + c] = v;
+        if (in && d >= 0) permuted[(int64_t)d * num_cols + c] = v;
       }
     }
   }
@@ -261,15 +264,17 @@ unpermute_fwd_kernel(const T* __restrict__ input, const int32_t* __restrict__ ro
       }
     }
   } else {
-    for (int64_t c = lane; c < num_cols; c += 32) {
+    for (int64_t c0 = 0; c0 < num_cols; c0 += 32) {
+      const int64_t c = c0 + lane;
+      const bool in = c < num_cols;
       float acc = 0.f;
       for (int k = 0; k < K; ++k) {
         const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
         const float p = __shfl_sync(0xffffffffu, p_lane, k);
-        if (s < 0) continue;
+        if (s < 0 || !in) continue;
         acc = __fadd_rn(acc, __fmul_rn(to_f32(input[(int64_t)s * num_cols + c]), p));
       }
-      dst[c] = from_f32<T>(acc);
+      if (in) dst[c] = from_f32<T>(acc);
     }
   }
 }
@@ -298,6 +303,14 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) dot[k] = 0.f;
   const T* g_row = grad_out + t * num_cols;
+  // Slot rows and probabilities, broadcast once (K <= KMAX <= 32).
+  int32_t src_k[KMAX];
+  float p_k[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    src_k[k] = __shfl_sync(0xffffffffu, src_lane, k);
+    p_k[k] = __shfl_sync(0xffffffffu, p_lane, k);
+  }
   if constexpr (VEC) {
     constexpr int NV = Vec16<T>::N;
     const int64_t nv = num_cols / NV;
@@ -307,8 +320,8 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k >= K) break;
-        const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
-        const float p = __shfl_sync(0xffffffffu, p_lane, k);
+        const int32_t s = src_k[k];
+        const float p = p_k[k];
         if (s < 0) continue;
         float v[NV];
         unpack16<T>(ld_stream(reinterpret_cast<const uint4*>(input + (int64_t)s * num_cols) + c), v);
@@ -327,8 +340,8 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k >= K) break;
-        const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
-        const float p = __shfl_sync(0xffffffffu, p_lane, k);
+        const int32_t s = src_k[k];
+        const float p = p_k[k];
         if (s < 0) continue;
         const float v = to_f32(input[(int64_t)s * num_cols + c]);
         dot[k] = fmaf(g, v, dot[k]);
