@@ -12,7 +12,8 @@ import threading
 import torch
 
 LIB_NAME = "libmoe_b200.so"
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+LIB_PATH = os.environ.get("MOE_B200_LIB") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 MOE_F32, MOE_F16, MOE_BF16 = 0, 1, 2
 _DTYPE_CODE = {torch.float32: MOE_F32, torch.float16: MOE_F16, torch.bfloat16: MOE_BF16}
