@@ -12,28 +12,41 @@
 //   kModeWgrad  (wgrad): Out[g] = X[rows of g]^T . Y[rows of g]  ([P, Q] per expert); the
 //               contraction runs over the ragged rows of expert g.  X and Y are MN-major.
 //
-// Warp roles (256 threads, one CTA per SM, persistent over a static tile stride):
-//   warp 0     TMA producer: fills a 4-stage shared-memory ring (A 128x64, B 256x64 per
-//              stage, 128-byte swizzle) and signals `full[s]` with the transaction bytes.
-//   warp 1     TMEM owner and MMA issuer: one elected thread issues 4 tcgen05.mma
-//              (M=128, N=256, K=16) per stage into one of two TMEM accumulators
-//              (2 x 256 fp32 columns) and commits each stage back to `empty[s]`.
-//   warps 4-7  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
-//              32*(w%4)..+31, i.e. output rows), round to the output dtype and store with
-//              16-byte vector stores, masking rows past the expert's end and columns past
-//              the output width.  Releasing the accumulator lets the MMA warp start the
-//              tile after next, so the epilogue overlaps the next tile's main loop.
+// and two CTA-group shapes:
+//   CG = 1  one CTA per tile, 128 x 256 tile, M=128 N=256 K=16 MMAs, 4 stages of 48 KB.
+//   CG = 2  a cluster of two CTAs (an SM pair) per 256 x 256 tile running cta_group::2
+//           MMAs (M=256, N=256): each CTA holds its own 128 rows of A and its own 128
+//           columns of B, so each SM streams 32 KB instead of 48 KB per 64-deep k-block;
+//           6 stages of 32 KB.  Only the pair's first CTA (the leader) issues MMAs.  Both
+//           CTAs load with TMA into their own shared memory; the loads complete their
+//           bytes on the leader's `full` barrier, which the leader alone arms with the
+//           pair's byte count.  The leader's commits arrive on both CTAs' `empty` and
+//           `tmem_full` barriers; both epilogues arrive on the leader's `tmem_empty` (the
+//           peer with a relaxed remote arrive).  No cluster-scope fence sits on the hot
+//           path: only a masked wgrad block hands its zeroed rows over with a
+//           release/acquire pair (`peer_done`).
+//
+// Warp roles (384 threads, one CTA per SM, persistent over a static tile stride):
+//   warp 0      TMA producer (one elected lane issues, the warp zero-fills masked rows).
+//   warp 1      TMEM owner; in the MMA-issuing CTA one lane issues 4 tcgen05.mma per
+//               stage into one of two TMEM accumulators (2 x 256 fp32 columns) and commits
+//               each stage back to the producers.
+//   warps 4-11  epilogue (8 warps, lane quarter = warp % 4, column half = (warp-4)/4):
+//               tcgen05.ld, round to the output dtype, transpose through a swizzled 2 KB
+//               shared buffer and store 64-byte row segments with row/column masks.
+//               Releasing the accumulator lets the MMA warp start the tile after next, so
+//               the epilogue overlaps the next tile's main loop.
 //
 // Ragged contraction (wgrad): the last 64-row block of an expert may reach into the next
-// expert's rows.  The producer loads that block on a private barrier, zeroes the rows
-// past the expert's end in shared memory (a swizzled 128-byte row stays one row), fences
-// the generic->async proxy and then arrives on `full[s]` itself.
+// expert's rows.  Each producer loads that block on a private barrier, zeroes the rows
+// past the expert's end in its shared memory (a swizzled 128-byte row stays one row),
+// fences the generic->async proxy and then hands the stage over.
 //
 // Tile scheduler: each CTA builds the per-expert tile prefix from `offsets` in shared
-// memory (no host sync), then walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...  Inside
-// an expert, tiles run row-block fastest so that the CTAs working at the same time share
-// the same B tile through L2.  Empty experts own no tile in kModeRows; in kModeWgrad they
-// own their full [P, Q] tiles, written as zeros.
+// memory (no host sync), then the cluster walks tiles c, c + #clusters, ...  Inside an
+// expert, tiles run row-block fastest so that concurrently running tiles share the same
+// B tile through L2.  Empty experts own no tile in kModeRows; in kModeWgrad they own
+// their full [P, Q] tiles, written as zeros.
 //
 // Every mbarrier wait is bounded (2 s); a wait that gives up sets a shared abort flag and
 // the device error word, every role then leaves its loop and the TMEM is freed.
@@ -47,44 +60,58 @@
 namespace moe {
 namespace gmm {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
-constexpr int STAGES = 4;
+constexpr int BN = 256;   // tile columns (both CTA-group shapes)
+constexpr int BMC = 128;  // tile rows held by one CTA
+constexpr int BK = 64;    // 64 x 16-bit = one 128-byte swizzle row
 constexpr int UMMA_K = 16;
-constexpr int kThreads = 256;
+constexpr int kEpiWarps = 8;  // warps 4..11
+constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kMaxGroups = 1024;
-constexpr uint32_t A_STAGE_BYTES = BM * BK * 2;
-constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;
-constexpr uint32_t STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr uint32_t kTmemCols = 2 * BN;
+constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 16-bit columns (swizzled 16-B chunks)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
+
+#ifndef MOE_GMM_EPI_EXPERIMENT
+#define MOE_GMM_EPI_EXPERIMENT 0  // 1: no global stores, 2: no epilogue work (timing probes)
+#endif
+
+template <int CG>
+struct Shape {
+  static constexpr int STAGES = CG == 1 ? 4 : 6;
+  static constexpr int TILE_M = BMC * CG;                     // rows of the tile (pair)
+  static constexpr int B_COLS = BN / CG;                      // B columns held by one CTA
+  static constexpr uint32_t A_BYTES = BMC * BK * 2;           // per CTA per stage
+  static constexpr uint32_t B_BYTES = B_COLS * BK * 2;        // per CTA per stage
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA per stage
+};
 
 enum Mode { kModeRows = 0, kModeWgrad = 1 };
 
+template <int CG>
 struct SmemLayout {
-  uint8_t a[STAGES][A_STAGE_BYTES];
-  uint8_t b[STAGES][B_STAGE_BYTES];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint8_t a[Shape<CG>::STAGES][Shape<CG>::A_BYTES];
+  uint8_t b[Shape<CG>::STAGES][Shape<CG>::B_BYTES];
+  uint8_t cbuf[kEpiWarps][kEpiBufBytes];  // epilogue transpose buffers (one per warp)
+  uint64_t full[Shape<CG>::STAGES];       // used in the leader CTA
+  uint64_t empty[Shape<CG>::STAGES];
   uint64_t tmem_full[2];
-  uint64_t tmem_empty[2];
+  uint64_t tmem_empty[2];                 // used in the leader CTA
   uint64_t aux;
+  uint64_t peer_done[Shape<CG>::STAGES];  // leader: the peer has zeroed its masked rows
   uint32_t tmem_base;
   int abort;
   int tile_prefix[kMaxGroups + 1];
-  int grp_start[kMaxGroups];
-  int grp_rows[kMaxGroups];
   int warp_sums[kThreads / 32];
 };
-constexpr size_t kSmemBytes = sizeof(SmemLayout) + 1024;  // + alignment slack
+template <int CG>
+constexpr size_t smem_bytes() { return sizeof(SmemLayout<CG>) + 1024; }  // + alignment slack
 
 struct Params {
   const int32_t* offsets;
   int offsets_plus_one;  // 1: offsets has E+1 entries starting at 0; 0: E end offsets
   int num_groups;
   int64_t m_total;       // rows of A / X / Y
-  int n_out;             // output columns per tile grid (kModeRows: Nout, kModeWgrad: Q)
+  int n_out;             // output columns (kModeRows: Nout, kModeWgrad: Q)
   int p_out;             // kModeWgrad: output rows per expert (P)
   int k_red;             // kModeRows: contraction length (Kc)
   void* out;             // kModeRows: C [m_total, n_out]; kModeWgrad: [E, p_out, n_out]
@@ -92,35 +119,54 @@ struct Params {
 
 struct TileInfo {
   int g;       // expert
-  int m_blk;   // tile row block
-  int n_blk;   // tile column block
+  int m_blk;   // tile row block (TILE_M rows)
+  int n_blk;   // tile column block (BN columns)
   int row0;    // kModeRows: first A row of the tile; kModeWgrad: first row of the expert
-  int rows;    // kModeRows: valid output rows; kModeWgrad: rows of the expert
-  int nkb;     // number of 64-wide contraction blocks
+  int rows;    // kModeRows: valid output rows of the tile; kModeWgrad: rows of the expert
+  int nkb;     // number of 64-deep contraction blocks
 };
 
-template <int MODE>
-__device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const Params& p, int t) {
+// First row and row count of expert g (negative counts clamp to zero).
+__device__ __forceinline__ void group_range(const Params& p, int g, int& start, int& rows) {
+  int st, en;
+  if (p.offsets_plus_one) { st = __ldg(p.offsets + g); en = __ldg(p.offsets + g + 1); }
+  else { st = g > 0 ? __ldg(p.offsets + g - 1) : 0; en = __ldg(p.offsets + g); }
+  start = st;
+  rows = en > st ? en - st : 0;
+}
+
+template <int MODE, int CG>
+__device__ __forceinline__ int tiles_of_group(const Params& p, int rows) {
+  constexpr int TM = Shape<CG>::TILE_M;
+  const int nt = (p.n_out + BN - 1) / BN;
+  if (MODE == kModeRows) return ((rows + TM - 1) / TM) * nt;
+  return ((p.p_out + TM - 1) / TM) * nt;
+}
+
+template <int MODE, int CG>
+__device__ __forceinline__ TileInfo decode_tile(const int* tile_prefix, const Params& p, int t) {
+  constexpr int TM = Shape<CG>::TILE_M;
   // Largest g with tile_prefix[g] <= t; experts that own no tile are skipped because
   // their prefix equals the next expert's.
   int lo = 0, hi = p.num_groups - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (s.tile_prefix[mid] <= t) lo = mid; else hi = mid - 1;
+    if (tile_prefix[mid] <= t) lo = mid; else hi = mid - 1;
   }
   TileInfo ti;
   ti.g = lo;
-  const int local = t - s.tile_prefix[lo];
-  const int start = s.grp_start[lo], rows = s.grp_rows[lo];
+  const int local = t - tile_prefix[lo];
+  int start, rows;
+  group_range(p, lo, start, rows);
   if (MODE == kModeRows) {
-    const int mt = (rows + BM - 1) / BM;
+    const int mt = (rows + TM - 1) / TM;
     ti.m_blk = local % mt;
     ti.n_blk = local / mt;
-    ti.row0 = start + ti.m_blk * BM;
-    ti.rows = min(BM, rows - ti.m_blk * BM);
+    ti.row0 = start + ti.m_blk * TM;
+    ti.rows = min(TM, rows - ti.m_blk * TM);
     ti.nkb = (p.k_red + BK - 1) / BK;
   } else {
-    const int pt = (p.p_out + BM - 1) / BM;
+    const int pt = (p.p_out + TM - 1) / TM;
     ti.m_blk = local % pt;
     ti.n_blk = local / pt;
     ti.row0 = start;
@@ -128,13 +174,6 @@ __device__ __forceinline__ TileInfo decode_tile(const SmemLayout& s, const Param
     ti.nkb = (rows + BK - 1) / BK;
   }
   return ti;
-}
-
-template <int MODE>
-__device__ __forceinline__ int tiles_of_group(const Params& p, int rows) {
-  const int nt = (p.n_out + BN - 1) / BN;
-  if (MODE == kModeRows) return ((rows + BM - 1) / BM) * nt;
-  return ((p.p_out + BM - 1) / BM) * nt;
 }
 
 // Packs 8 fp32 values into 8 16-bit values (round to nearest even) as one 16-byte vector.
@@ -155,27 +194,42 @@ __device__ __forceinline__ uint4 pack8_16b(const uint32_t* v) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Pipeline waits are CTA-scope acquires: data hand-offs between the two CTAs of a pair
+// are ordered by TMA transaction counts and tcgen05 commits, not by generic memory.
+__device__ __forceinline__ bool wait_local(uint32_t bar, uint32_t parity, volatile int* abort) {
+  return ptx::wait_bounded(bar, parity, abort, kWaitTimeoutNs);
+}
+
 // A_MN / B_MN: the operand is MN-major in global memory (and in shared memory).
 // In kModeRows map_b is 3-D (inner, outer, expert); every other map is 2-D (inner, row).
-template <int MODE, int AB_FORMAT, bool A_MN, bool B_MN, typename OutT>
+// Tensor-map boxes: A 64 x 128 (K-major) or 64 x 64 (MN-major, 2 per CTA); B 64 x B_COLS
+// (K-major) or 64 x 64 (MN-major, B_COLS / 64 per CTA).
+template <int MODE, int CG, int AB_FORMAT, bool A_MN, bool B_MN, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
 gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                  const Params p) {
+  using Sh = Shape<CG>;
+  constexpr int STAGES = Sh::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  SmemLayout& s = *reinterpret_cast<SmemLayout*>(
+  SmemLayout<CG>& s = *reinterpret_cast<SmemLayout<CG>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &s.abort;
+  const uint32_t rank = CG == 1 ? 0u : ptx::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x / CG;
+  const int num_clusters = gridDim.x / CG;
 
   // ------------------------------------------------------------ prologue
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
       ptx::mbar_init(ptx::smem_u32(&s.full[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&s.empty[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&s.peer_done[i]), 1);
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(ptx::smem_u32(&s.tmem_full[i]), 1);
-      ptx::mbar_init(ptx::smem_u32(&s.tmem_empty[i]), 4);
+      ptx::mbar_init(ptx::smem_u32(&s.tmem_empty[i]), CG * kEpiWarps);
     }
     ptx::mbar_init(ptx::smem_u32(&s.aux), 1);
     s.abort = 0;
@@ -186,12 +240,12 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     ptx::prefetch_tensormap(&map_b);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(ptx::smem_u32(&s.tmem_base), kTmemCols);
-    ptx::tmem_relinquish();
+    ptx::tmem_alloc<CG>(ptx::smem_u32(&s.tmem_base), kTmemCols);
+    ptx::tmem_relinquish<CG>();
   }
-  // Per-expert rows and tile prefix (block-wide scan; each thread owns 4 experts).
+  // Per-expert tile prefix (block-wide scan; each thread owns up to PER experts).
   {
-    constexpr int PER = kMaxGroups / kThreads;
+    constexpr int PER = (kMaxGroups + kThreads - 1) / kThreads;
     const int g0 = threadIdx.x * PER;
     int cnt[PER];
     int local_sum = 0;
@@ -200,14 +254,9 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const int g = g0 + i;
       cnt[i] = 0;
       if (g < p.num_groups) {
-        int st, en;
-        if (p.offsets_plus_one) { st = p.offsets[g]; en = p.offsets[g + 1]; }
-        else { st = g > 0 ? p.offsets[g - 1] : 0; en = p.offsets[g]; }
-        int rows = en - st;
-        if (rows < 0) rows = 0;
-        s.grp_start[g] = st;
-        s.grp_rows[g] = rows;
-        cnt[i] = tiles_of_group<MODE>(p, rows);
+        int st, rows;
+        group_range(p, g, st, rows);
+        cnt[i] = tiles_of_group<MODE, CG>(p, rows);
       }
       local_sum += cnt[i];
     }
@@ -232,6 +281,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
   }
   ptx::tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();  // peer barriers are initialised
   ptx::tc_fence_after();
   const int total_tiles = s.tile_prefix[p.num_groups];
   const uint32_t tmem_base = s.tmem_base;
@@ -240,70 +290,110 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     // ---------------------------------------------------------- TMA producer
     int stage = 0;
     uint32_t phase = 0, aux_phase = 0;
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
-      const TileInfo ti = decode_tile<MODE>(s, p, t);
+    uint32_t peer_phase_bits = 0;  // leader: per-stage parity of peer_done
+    for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
+      const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
       for (int kb = 0; kb < ti.nkb; ++kb) {
-        if (!ptx::wait_bounded(ptx::smem_u32(&s.empty[stage]), phase ^ 1, abort_flag,
-                               kWaitTimeoutNs))
-          break;
+        if (!wait_local(ptx::smem_u32(&s.empty[stage]), phase ^ 1, abort_flag)) break;
         const uint32_t sa = ptx::smem_u32(&s.a[stage][0]);
         const uint32_t sb = ptx::smem_u32(&s.b[stage][0]);
-        if (MODE == kModeRows) {
+        // The leader's full barrier, addressed for the cluster.
+        const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
+        const uint32_t full_c = CG == 1 ? full_local : ptx::mapa_shared(full_local, 0);
+        bool masked = false;
+        int valid = BK;
+        int r0 = 0;
+        if (MODE == kModeWgrad) {
+          r0 = ti.row0 + kb * BK;
+          valid = ti.row0 + ti.rows - r0;  // rows of this block inside the expert
+          masked = valid < BK;
+        }
+        if (!masked) {
           if (lane == 0) {
-            const uint32_t fb = ptx::smem_u32(&s.full[stage]);
-            ptx::mbar_arrive_expect_tx(fb, STAGE_BYTES);
-            const int k0 = kb * BK;
-            ptx::tma_load_2d(sa, &map_a, fb, k0, ti.row0);
-            if (!B_MN) {
-              ptx::tma_load_3d(sb, &map_b, fb, k0, ti.n_blk * BN, ti.g);
-            } else {
+            // The leader expects the bytes of both CTAs; the peer's loads complete their
+            // bytes on the leader's barrier (possibly before this expect, which is fine:
+            // the phase cannot complete before the leader's single arrival).
+            if (leader) ptx::mbar_arrive_expect_tx(full_local, CG * Sh::STAGE_BYTES);
+            auto ld2 = [&](uint32_t dst, const CUtensorMap* m, int c0, int c1) {
+              if (CG == 1) ptx::tma_load_2d(dst, m, full_c, c0, c1);
+              else ptx::tma_load_2d_pair(dst, m, full_c, c0, c1);
+            };
+            auto ld3 = [&](uint32_t dst, const CUtensorMap* m, int c0, int c1, int c2) {
+              if (CG == 1) ptx::tma_load_3d(dst, m, full_c, c0, c1, c2);
+              else ptx::tma_load_3d_pair(dst, m, full_c, c0, c1, c2);
+            };
+            if (MODE == kModeRows) {
+              const int k0 = kb * BK;
+              ld2(sa, &map_a, k0, ti.row0 + (int)rank * BMC);
+              const int nb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+              if (!B_MN) {
+                ld3(sb, &map_b, k0, nb, ti.g);
+              } else {
 #pragma unroll
-              for (int j = 0; j < BN / 64; ++j)
-                ptx::tma_load_3d(sb + j * (BK * 128), &map_b, fb, ti.n_blk * BN + j * 64, k0, ti.g);
+                for (int j = 0; j < Sh::B_COLS / 64; ++j)
+                  ld3(sb + j * (BK * 128), &map_b, nb + j * 64, k0, ti.g);
+              }
+            } else {
+              const int pa = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
+              const int qb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+#pragma unroll
+              for (int j = 0; j < BMC / 64; ++j) ld2(sa + j * (BK * 128), &map_a, pa + j * 64, r0);
+#pragma unroll
+              for (int j = 0; j < Sh::B_COLS / 64; ++j)
+                ld2(sb + j * (BK * 128), &map_b, qb + j * 64, r0);
             }
           }
         } else {
-          const int r0 = ti.row0 + kb * BK;
-          const int valid = ti.row0 + ti.rows - r0;  // rows of this block inside the expert
-          const bool masked = valid < BK;
-          const uint32_t fb = ptx::smem_u32(&s.full[stage]);
-          const uint32_t lb = masked ? ptx::smem_u32(&s.aux) : fb;
+          // Masked wgrad block: load locally, zero the rows past the expert, hand over.
+          const uint32_t ab = ptx::smem_u32(&s.aux);
           if (lane == 0) {
-            ptx::mbar_arrive_expect_tx(lb, STAGE_BYTES);
+            ptx::mbar_arrive_expect_tx(ab, Sh::STAGE_BYTES);
+            const int pa = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
+            const int qb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j)
-              ptx::tma_load_2d(sa + j * (BK * 128), &map_a, lb, ti.m_blk * BM + j * 64, r0);
+            for (int j = 0; j < BMC / 64; ++j)
+              ptx::tma_load_2d(sa + j * (BK * 128), &map_a, ab, pa + j * 64, r0);
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              ptx::tma_load_2d(sb + j * (BK * 128), &map_b, lb, ti.n_blk * BN + j * 64, r0);
+            for (int j = 0; j < Sh::B_COLS / 64; ++j)
+              ptx::tma_load_2d(sb + j * (BK * 128), &map_b, ab, qb + j * 64, r0);
           }
-          if (masked) {
-            __syncwarp();
-            const bool ok = ptx::wait_bounded(lb, aux_phase, abort_flag, kWaitTimeoutNs);
-            aux_phase ^= 1;
-            if (!ok) break;
-            // Zero rows [valid, BK) of every 64-column box (2 A boxes + 4 B boxes).
-            const int zrows = BK - valid;
-            const int n16 = zrows * 8;  // 16-byte chunks per box
-            for (int box = 0; box < (BM + BN) / 64; ++box) {
-              uint8_t* base = box < BM / 64 ? &s.a[stage][box * BK * 128]
-                                            : &s.b[stage][(box - BM / 64) * BK * 128];
-              for (int i = lane; i < n16; i += 32) {
-                reinterpret_cast<uint4*>(base + valid * 128)[i] = make_uint4(0, 0, 0, 0);
-              }
-            }
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(fb);
+          __syncwarp();
+          const bool ok = ptx::wait_bounded(ab, aux_phase, abort_flag, kWaitTimeoutNs);
+          aux_phase ^= 1;
+          if (!ok) break;
+          const int n16 = (BK - valid) * 8;  // 16-byte chunks to clear per 64-column box
+          constexpr int kBoxes = (BMC + Sh::B_COLS) / 64;
+          for (int box = 0; box < kBoxes; ++box) {
+            uint8_t* base = box < BMC / 64 ? &s.a[stage][box * BK * 128]
+                                           : &s.b[stage][(box - BMC / 64) * BK * 128];
+            for (int i = lane; i < n16; i += 32)
+              reinterpret_cast<uint4*>(base + valid * 128)[i] = make_uint4(0, 0, 0, 0);
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (CG == 1) {
+            if (lane == 0) ptx::mbar_arrive(full_local);
+          } else if (!leader) {
+            // Release the zeroed rows to the leader, which then arms `full` for both.
+            if (lane == 0)
+              ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&s.peer_done[stage]), 0));
+          } else {
+            const uint32_t pd = ptx::smem_u32(&s.peer_done[stage]);
+            const bool ok2 = ptx::wait_bounded_cluster(pd, (peer_phase_bits >> stage) & 1u,
+                                                       abort_flag, kWaitTimeoutNs);
+            peer_phase_bits ^= 1u << stage;
+            if (!ok2) break;
+            if (lane == 0) ptx::mbar_arrive(full_local);
           }
         }
         __syncwarp();
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 && leader) {
     // ---------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = ptx::make_idesc_f16(AB_FORMAT, A_MN ? 1 : 0, B_MN ? 1 : 0, BM, BN);
+    constexpr uint32_t idesc =
+        ptx::make_idesc_f16(AB_FORMAT, A_MN ? 1 : 0, B_MN ? 1 : 0, Sh::TILE_M, BN);
     // K-major: rows of 128 bytes, 8-row atoms 1024 bytes apart; a K=16 step is +32 bytes.
     // MN-major: 64-element column chunks BK*128 bytes apart (LBO), 8-k-row atoms 1024
     // bytes apart (SBO); a K=16 step is two atoms (+2048 bytes).
@@ -311,18 +401,16 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++acc) {
-      const TileInfo ti = decode_tile<MODE>(s, p, t);
+    for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters, ++acc) {
+      const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
       const int buf = acc & 1;
       const uint32_t acc_phase = (acc >> 1) & 1;
-      if (!ptx::wait_bounded(ptx::smem_u32(&s.tmem_empty[buf]), acc_phase ^ 1, abort_flag,
-                             kWaitTimeoutNs))
-        break;
+      if (!wait_local(ptx::smem_u32(&s.tmem_empty[buf]), acc_phase ^ 1, abort_flag)) break;
       ptx::tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * BN;
       bool ok = true;
       for (int kb = 0; kb < ti.nkb; ++kb) {
-        if (!ptx::wait_bounded(ptx::smem_u32(&s.full[stage]), phase, abort_flag, kWaitTimeoutNs)) {
+        if (!wait_local(ptx::smem_u32(&s.full[stage]), phase, abort_flag)) {
           ok = false;
           break;
         }
@@ -336,75 +424,121 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                                      : ptx::make_sw128_desc(sa + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? ptx::make_sw128_desc(sb + kk * 2048, kLboMN, 1024)
                                      : ptx::make_sw128_desc(sb + kk * 32, 16, 1024);
-            ptx::mma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            ptx::mma_f16_ss<CG>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
-          ptx::mma_commit(ptx::smem_u32(&s.empty[stage]));
+          const uint32_t eb = ptx::smem_u32(&s.empty[stage]);
+          ptx::mma_commit<CG>(eb);
+          if (CG == 2) ptx::mma_commit<CG>(ptx::mapa_shared(eb, 1));
         }
         __syncwarp();
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
       if (lane == 0) {
-        if (ti.nkb > 0) ptx::mma_commit(ptx::smem_u32(&s.tmem_full[buf]));
-        else ptx::mbar_arrive(ptx::smem_u32(&s.tmem_full[buf]));
+        const uint32_t fb = ptx::smem_u32(&s.tmem_full[buf]);
+        if (ti.nkb > 0) {
+          ptx::mma_commit<CG>(fb);
+          if (CG == 2) ptx::mma_commit<CG>(ptx::mapa_shared(fb, 1));
+        } else {
+          ptx::mbar_arrive(fb);
+          if (CG == 2) ptx::mbar_arrive_relaxed_cluster(ptx::mapa_shared(fb, 1));
+        }
       }
       __syncwarp();
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // accumulator row owned by this thread
+    // Warp w reads TMEM lanes 32*(w%4)..+31 (this CTA's tile rows) and columns
+    // [128*h, 128*h+128), h = (w-4)/4, in four 32-column chunks.  Each chunk is rounded to
+    // 16 bits, written row-per-lane into a 2 KB buffer (16-byte chunks XOR-swizzled so both
+    // the row-wise writes and the column-wise reads are conflict-free), read back so that
+    // every store instruction writes eight full 64-byte row segments, and stored with a
+    // row/column mask.  The next chunk's TMEM load is issued before the current chunk is
+    // stored.
+    const int ew = warp - 4;
+    const int q = ew & 3, h = ew >> 2;
     OutT* out = static_cast<OutT*>(p.out);
+    uint8_t* cbuf = s.cbuf[ew];
+    const int wr_row = lane;        // row written by this lane
+    const int rd_chunk = lane & 3;  // 16-byte chunk read by this lane
+    const int rd_row0 = lane >> 2;  // first row read by this lane (then +8, +16, +24)
     int acc = 0;
-    for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++acc) {
-      const TileInfo ti = decode_tile<MODE>(s, p, t);
+    for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters, ++acc) {
+      const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
       const int buf = acc & 1;
       const uint32_t acc_phase = (acc >> 1) & 1;
-      if (!ptx::wait_bounded(ptx::smem_u32(&s.tmem_full[buf]), acc_phase, abort_flag,
-                             kWaitTimeoutNs))
-        break;
+      if (!wait_local(ptx::smem_u32(&s.tmem_full[buf]), acc_phase, abort_flag)) break;
       ptx::tc_fence_after();
       const int n0 = ti.n_blk * BN;
+      const int col_lo = h * (BN / 2);
       const int valid_cols = min(BN, p.n_out - n0);
       int valid_rows;
-      OutT* row_ptr;
+      OutT* tile_ptr;  // element (0, 0) of this CTA's 128 rows of the tile
       if (MODE == kModeRows) {
-        valid_rows = ti.rows;
-        row_ptr = out + (int64_t)(ti.row0 + r) * p.n_out + n0;
+        valid_rows = min(BMC, ti.rows - (int)rank * BMC);
+        tile_ptr = out + (int64_t)(ti.row0 + (int)rank * BMC) * p.n_out + n0;
       } else {
-        valid_rows = min(BM, p.p_out - ti.m_blk * BM);
-        row_ptr = out + ((int64_t)ti.g * p.p_out + ti.m_blk * BM + r) * p.n_out + n0;
+        const int prow = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
+        valid_rows = min(BMC, p.p_out - prow);
+        tile_ptr = out + ((int64_t)ti.g * p.p_out + prow) * p.n_out + n0;
       }
-      for (int c0 = 0; c0 < valid_cols; c0 += 32) {
-        uint32_t v[32];
-        if (ti.nkb > 0) {
-          ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + c0, v);
-          ptx::tmem_wait_ld();
+#if MOE_GMM_EPI_EXPERIMENT == 2
+      const int nchunks = 0;
+#else
+      const int nchunks = max(0, min(BN / 2, valid_cols - col_lo) + 31) / 32;
+#endif
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + col_lo;
+      uint32_t v[32];
+      const bool has_acc = ti.nkb > 0;
+      if (has_acc && nchunks > 0) {
+        ptx::tmem_ld_32x32b_x32(tbase, v);
+        ptx::tmem_wait_ld();
+      }
+      for (int c = 0; c < nchunks; ++c) {
+        uint32_t w[16];
+        if (has_acc) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const uint4 u = pack8_16b<OutT>(&v[i * 8]);
+            w[i * 4 + 0] = u.x; w[i * 4 + 1] = u.y; w[i * 4 + 2] = u.z; w[i * 4 + 3] = u.w;
+          }
+          if (c + 1 < nchunks) ptx::tmem_ld_32x32b_x32(tbase + (c + 1) * 32, v);
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0u;
+          for (int i = 0; i < 16; ++i) w[i] = 0u;
         }
-        if (r < valid_rows) {
-          if (c0 + 32 <= valid_cols) {
-            if constexpr (sizeof(OutT) == 2) {
-              uint4* dst = reinterpret_cast<uint4*>(row_ptr + c0);
 #pragma unroll
-              for (int i = 0; i < 4; ++i) dst[i] = pack8_16b<OutT>(&v[i * 8]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) row_ptr[c0 + i] = from_f32<OutT>(__uint_as_float(v[i]));
-            }
-          } else {
-            const int nc = valid_cols - c0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (i < nc) row_ptr[c0 + i] = from_f32<OutT>(__uint_as_float(v[i]));
-          }
+        for (int i = 0; i < 4; ++i) {
+          const int phys = i ^ ((wr_row >> 1) & 3);
+          *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
+              make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
         }
+        __syncwarp();
+        const int col = col_lo + c * 32 + rd_chunk * 8;  // first column of this lane's chunk
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = rd_row0 + i * 8;
+          const int phys = rd_chunk ^ ((rr >> 1) & 3);
+          const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
+          const int row = q * 32 + rr;
+#if MOE_GMM_EPI_EXPERIMENT == 0
+          if (row < valid_rows && col < valid_cols)
+            *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;
+#else
+          if (u.x == 0x7fc00001u && row < 0 && col < 0) *reinterpret_cast<uint4*>(tile_ptr) = u;
+#endif
+        }
+        __syncwarp();
+        if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&s.tmem_empty[buf]));
+      if (lane == 0) {
+        // TMEM reads are complete (tcgen05.wait::ld); the stores need no ordering here.
+        const uint32_t eb = ptx::smem_u32(&s.tmem_empty[buf]);
+        if (leader) ptx::mbar_arrive(eb);
+        else ptx::mbar_arrive_relaxed_cluster(ptx::mapa_shared(eb, 0));
+      }
     }
   }
 
@@ -416,9 +550,10 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     if (warp == 1) __nanosleep(100000);
     __syncwarp();
   }
+  if constexpr (CG == 2) ptx::cluster_sync();  // no remote arrivals target this CTA any more
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, kTmemCols);
+    ptx::tmem_dealloc<CG>(tmem_base, kTmemCols);
   }
 }
 

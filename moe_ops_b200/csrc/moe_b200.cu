@@ -3,9 +3,11 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -90,23 +92,68 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, con
 }
 
 // ---------------------------------------------------------------- GEMM launchers
-template <int MODE, int FMT, bool A_MN, bool B_MN, typename OutT>
+template <int MODE, int CG, int FMT, bool A_MN, bool B_MN, typename OutT>
 static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const gmm::Params& p,
                         cudaStream_t stream) {
-  auto kern = gmm::gmm_sm100_kernel<MODE, FMT, A_MN, B_MN, OutT>;
+  auto kern = gmm::gmm_sm100_kernel<MODE, CG, FMT, A_MN, B_MN, OutT>;
   const int dev = current_device();
-  static unsigned long long attr_set = 0;  // per-device bitmask
+  static unsigned long long attr_set = 0;  // per-device bitmask, one per instantiation
+  static int max_clusters[64] = {0};
   if (dev < 64 && !(attr_set & (1ull << dev))) {
     MOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)gmm::kSmemBytes));
+                                        (int)gmm::smem_bytes<CG>()));
     attr_set |= 1ull << dev;
   }
-  kern<<<num_sms(dev), gmm::kThreads, gmm::kSmemBytes, stream>>>(ma, mb, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(gmm::kThreads);
+  cfg.dynamicSmemBytes = gmm::smem_bytes<CG>();
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG == 2 ? 1 : 0;
+  // A persistent kernel strides tiles statically, so every CTA must be resident at once:
+  // for SM pairs the grid is the number of clusters that fit together (cluster placement
+  // is per GPC, so it can be below #SMs / 2).
+  int grid = (num_sms(dev) / CG) * CG;
+  if (CG == 2 && dev < 64) {
+    if (max_clusters[dev] == 0) {
+      cfg.gridDim = dim3(grid);
+      int n = 0;
+      MOE_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      max_clusters[dev] = n > 0 ? n : 1;
+    }
+    grid = std::min(grid, max_clusters[dev] * CG);
+  }
+  cfg.gridDim = dim3(grid);
+  if (getenv("MOE_B200_DEBUG"))
+    fprintf(stderr, "[moe_b200] gmm launch: mode=%d cg=%d grid=%d smem=%zu\n", MODE, CG, grid,
+            gmm::smem_bytes<CG>());
+  MOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, p));
   MOE_LAUNCH_CHECK();
   return MOE_OK;
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// CTA-group choice: MOE_B200_GMM_CG=1|2 forces it (tuning/tests); otherwise `auto_cg`.
+static int pick_cg(int auto_cg) {
+  const char* e = getenv("MOE_B200_GMM_CG");
+  return (e && (e[0] == '1' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : auto_cg;
+}
+
+template <int MODE, bool A_MN, bool B_MN>
+static int launch_fmt_cg(int dtype, int cg, const CUtensorMap& ma, const CUtensorMap& mb,
+                         const gmm::Params& p, cudaStream_t stream) {
+  if (dtype == MOE_BF16)
+    return cg == 2 ? launch_sm100<MODE, 2, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, p, stream)
+                   : launch_sm100<MODE, 1, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, p, stream);
+  return cg == 2 ? launch_sm100<MODE, 2, 0, A_MN, B_MN, __half>(ma, mb, p, stream)
+                 : launch_sm100<MODE, 1, 0, A_MN, B_MN, __half>(ma, mb, p, stream);
+}
 
 // Row mode (forward / dgrad): C[m_total, n_out] = A[m_total, k_red] . op(B[g]).
 // b_mn: B[g] stored [k_red, n_out] (MN-major) instead of [n_out, k_red].
@@ -142,16 +189,20 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     MOE_LAUNCH_CHECK();
     return MOE_OK;
   }
+  // SM pairs (256-row tiles) pay off when experts have many rows; with few rows per
+  // expert the 128-row tiles waste less of the last, partial tile.
+  const int cg = pick_cg(m_total >= 384ll * E ? 2 : 1);
+  const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
     const uint64_t dims[2] = {(uint64_t)k_red, (uint64_t)m_total};
-    const uint32_t box[2] = {(uint32_t)gmm::BK, (uint32_t)gmm::BM};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, (uint32_t)gmm::BMC};
     int rc = make_map(&ma, A, dtype, 2, dims, box);
     if (rc) return rc;
   }
   if (!b_mn) {
     const uint64_t dims[3] = {(uint64_t)k_red, (uint64_t)n_out, (uint64_t)E};
-    const uint32_t box[3] = {(uint32_t)gmm::BK, (uint32_t)gmm::BN, 1};
+    const uint32_t box[3] = {(uint32_t)gmm::BK, b_cols, 1};
     int rc = make_map(&mb, B, dtype, 3, dims, box);
     if (rc) return rc;
   } else {
@@ -169,12 +220,8 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   p.p_out = 0;
   p.k_red = (int)k_red;
   p.out = C;
-  if (dtype == MOE_BF16) {
-    return b_mn ? launch_sm100<gmm::kModeRows, 1, false, true, __nv_bfloat16>(ma, mb, p, stream)
-                : launch_sm100<gmm::kModeRows, 1, false, false, __nv_bfloat16>(ma, mb, p, stream);
-  }
-  return b_mn ? launch_sm100<gmm::kModeRows, 0, false, true, __half>(ma, mb, p, stream)
-              : launch_sm100<gmm::kModeRows, 0, false, false, __half>(ma, mb, p, stream);
+  return b_mn ? launch_fmt_cg<gmm::kModeRows, false, true>(dtype, cg, ma, mb, p, stream)
+              : launch_fmt_cg<gmm::kModeRows, false, false>(dtype, cg, ma, mb, p, stream);
 }
 
 // Wgrad mode: Out[g] [P, Q] = X[rows of g]^T . Y[rows of g]; X [m_total, P], Y [m_total, Q].
@@ -205,6 +252,7 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
     MOE_LAUNCH_CHECK();
     return MOE_OK;
   }
+  const int cg = pick_cg(P > gmm::BMC ? 2 : 1);
   CUtensorMap mx, my;
   {
     const uint64_t dims[2] = {(uint64_t)P, (uint64_t)m_total};
@@ -227,9 +275,7 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
   p.p_out = (int)P;
   p.k_red = 0;
   p.out = Out;
-  if (dtype == MOE_BF16)
-    return launch_sm100<gmm::kModeWgrad, 1, true, true, __nv_bfloat16>(mx, my, p, stream);
-  return launch_sm100<gmm::kModeWgrad, 0, true, true, __half>(mx, my, p, stream);
+  return launch_fmt_cg<gmm::kModeWgrad, true, true>(dtype, cg, mx, my, p, stream);
 }
 
 static int check_gmm_args(const void* a, const void* b, const void* c, const int32_t* offsets,

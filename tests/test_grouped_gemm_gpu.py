@@ -15,6 +15,16 @@ pytestmark = pytest.mark.gpu
 TOL = {torch.bfloat16: 1e-2, torch.float16: 2e-3, torch.float32: 1e-5}
 
 
+@pytest.fixture(params=["auto", "1", "2"])
+def cta_group(request, monkeypatch):
+    """Runs a test with the automatic CTA-group choice, single-CTA tiles and SM-pair tiles."""
+    if request.param != "auto":
+        monkeypatch.setenv("MOE_B200_GMM_CG", request.param)
+    else:
+        monkeypatch.delenv("MOE_B200_GMM_CG", raising=False)
+    return request.param
+
+
 def _offsets(sizes):
     off = torch.zeros(len(sizes) + 1, dtype=torch.int32)
     off[1:] = torch.tensor(sizes, dtype=torch.int64).cumsum(0).to(torch.int32)
@@ -68,12 +78,12 @@ def test_golden_fp32(cuda_dev, name):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("trans_b", [True, False])
-def test_small_ragged(cuda_dev, dtype, trans_b):
+def test_small_ragged(cuda_dev, cta_group, dtype, trans_b):
     _run([5, 0, 17, 300, 129, 128, 1, 0], K=192, N=264, dtype=dtype, trans_b=trans_b, seed=1)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_partial_tiles(cuda_dev, dtype):
+def test_partial_tiles(cuda_dev, cta_group, dtype):
     # The deprecated partial-tile test's row counts (develop/deprecated/test_grouped_gemm.py
     # :227-253), with N=200 and K=136 (multiples of 8 keep the TMA path).
     _run([100, 250, 130, 300], K=136, N=200, dtype=dtype, seed=2)
@@ -85,7 +95,7 @@ def test_unaligned_falls_back_to_cuda_cores(cuda_dev):
     _run([100, 250, 130, 300], K=130, N=202, dtype=torch.bfloat16, seed=4)
 
 
-def test_end_offsets_form(cuda_dev):
+def test_end_offsets_form(cuda_dev, cta_group):
     _run([64, 0, 200, 33], K=256, N=256, dtype=torch.bfloat16, seed=5, end_offsets=True)
 
 
@@ -93,7 +103,7 @@ def test_fp32(cuda_dev):
     _run([10, 0, 70, 33], K=96, N=80, dtype=torch.float32, seed=6)
 
 
-def test_all_empty(cuda_dev):
+def test_all_empty(cuda_dev, cta_group):
     dev = cuda_dev
     A = torch.randn(0, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
     B = torch.randn(4, 128, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
@@ -104,12 +114,12 @@ def test_all_empty(cuda_dev):
     assert (B.grad == 0).all()
 
 
-def test_cfg2_uniform(cuda_dev):
+def test_cfg2_uniform(cuda_dev, cta_group):
     # Config 2: A [16384, 4096], B [16, 4096, 4096], 1024 rows per expert.
     _run([1024] * 16, K=4096, N=4096, dtype=torch.bfloat16, seed=7)
 
 
-def test_cfg2_zipf(cuda_dev):
+def test_cfg2_zipf(cuda_dev, cta_group):
     # Config 2 variant: Zipf(s=1.1) sizes summing to 16384 with 2 empty experts.
     w = 1.0 / torch.arange(1, 15).double() ** 1.1
     sizes = (w / w.sum() * 16384).floor().long().tolist()
@@ -119,6 +129,6 @@ def test_cfg2_zipf(cuda_dev):
     _run(sizes, K=4096, N=4096, dtype=torch.bfloat16, seed=8)
 
 
-def test_deep_contraction_wgrad(cuda_dev):
+def test_deep_contraction_wgrad(cuda_dev, cta_group):
     # One expert with many rows: long ragged contraction in wgrad.
     _run([7000, 3, 1000], K=512, N=768, dtype=torch.bfloat16, seed=9)
