@@ -27,20 +27,22 @@
 //           release/acquire pair (`peer_done`).
 //
 // Warp roles (384 threads, one CTA per SM, persistent over a static tile stride):
-//   warp 0      TMA producer (one elected lane issues, the warp zero-fills masked rows).
+//   warp 0      TMA producer (one elected lane issues; it never waits on data).
+//   warp 2      wgrad only: zero-fills the rows of masked blocks (see below).
 //   warp 1      TMEM owner; in the MMA-issuing CTA one lane issues 4 tcgen05.mma per
 //               stage into one of two TMEM accumulators (2 x 256 fp32 columns) and commits
 //               each stage back to the producers.
 //   warps 4-11  epilogue (8 warps, lane quarter = warp % 4, column half = (warp-4)/4):
-//               tcgen05.ld, round to the output dtype, transpose through a swizzled 2 KB
-//               shared buffer and store 64-byte row segments with row/column masks.
+//               tcgen05.ld, round to the output dtype, stage 32 x 32 blocks in a 2 KB
+//               buffer laid out in the TMA 64-byte swizzle and write them with TMA stores
+//               (or, for row tiles that end inside an expert, masked 64-byte row stores).
 //               Releasing the accumulator lets the MMA warp start the tile after next, so
 //               the epilogue overlaps the next tile's main loop.
 //
 // Ragged contraction (wgrad): the last 64-row block of an expert may reach into the next
-// expert's rows.  Each producer loads that block on a private barrier, zeroes the rows
-// past the expert's end in its shared memory (a swizzled 128-byte row stays one row),
-// fences the generic->async proxy and then hands the stage over.
+// expert's rows.  The producer loads that block on the stage's `raw` barrier and moves on;
+// the fix-up warp waits for it, zeroes the rows past the expert's end in shared memory,
+// fences the generic->async proxy and then hands the stage to the MMA.
 //
 // Tile scheduler: each CTA builds the per-expert tile prefix from `offsets` in shared
 // memory (no host sync), then the cluster walks tiles c, c + #clusters, ...  Inside an
@@ -96,7 +98,7 @@ struct SmemLayout {
   uint64_t empty[Shape<CG>::STAGES];
   uint64_t tmem_full[2];
   uint64_t tmem_empty[2];                 // used in the leader CTA
-  uint64_t aux;
+  uint64_t raw[Shape<CG>::STAGES];        // masked wgrad block landed (before zeroing)
   uint64_t peer_done[Shape<CG>::STAGES];  // leader: the peer has zeroed its masked rows
   uint32_t tmem_base;
   int abort;
@@ -207,7 +209,7 @@ __device__ __forceinline__ bool wait_local(uint32_t bar, uint32_t parity, volati
 template <int MODE, int CG, int AB_FORMAT, bool A_MN, bool B_MN, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
 gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const Params p) {
+                 const __grid_constant__ CUtensorMap map_c, const Params p) {
   using Sh = Shape<CG>;
   constexpr int STAGES = Sh::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -226,18 +228,19 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       ptx::mbar_init(ptx::smem_u32(&s.full[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&s.empty[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&s.peer_done[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&s.raw[i]), 1);
     }
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(ptx::smem_u32(&s.tmem_full[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&s.tmem_empty[i]), CG * kEpiWarps);
     }
-    ptx::mbar_init(ptx::smem_u32(&s.aux), 1);
     s.abort = 0;
     ptx::fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&map_a);
     ptx::prefetch_tensormap(&map_b);
+    ptx::prefetch_tensormap(&map_c);
   }
   if (warp == 1) {
     ptx::tmem_alloc<CG>(ptx::smem_u32(&s.tmem_base), kTmemCols);
@@ -288,78 +291,90 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 
   if (warp == 0) {
     // ---------------------------------------------------------- TMA producer
+    // Never waits on data: a masked wgrad block is loaded on the stage's `raw` barrier and
+    // handed to the fix-up warp, the producer moves on to the next stage.
     int stage = 0;
-    uint32_t phase = 0, aux_phase = 0;
-    uint32_t peer_phase_bits = 0;  // leader: per-stage parity of peer_done
+    uint32_t phase = 0;
     for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
       const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
       for (int kb = 0; kb < ti.nkb; ++kb) {
         if (!wait_local(ptx::smem_u32(&s.empty[stage]), phase ^ 1, abort_flag)) break;
-        const uint32_t sa = ptx::smem_u32(&s.a[stage][0]);
-        const uint32_t sb = ptx::smem_u32(&s.b[stage][0]);
-        // The leader's full barrier, addressed for the cluster.
-        const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
-        const uint32_t full_c = CG == 1 ? full_local : ptx::mapa_shared(full_local, 0);
-        bool masked = false;
-        int valid = BK;
-        int r0 = 0;
-        if (MODE == kModeWgrad) {
-          r0 = ti.row0 + kb * BK;
-          valid = ti.row0 + ti.rows - r0;  // rows of this block inside the expert
-          masked = valid < BK;
-        }
-        if (!masked) {
-          if (lane == 0) {
+        if (lane == 0) {
+          const uint32_t sa = ptx::smem_u32(&s.a[stage][0]);
+          const uint32_t sb = ptx::smem_u32(&s.b[stage][0]);
+          // The leader's full barrier, addressed for the cluster.
+          const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
+          const uint32_t full_c = CG == 1 ? full_local : ptx::mapa_shared(full_local, 0);
+          if (MODE == kModeRows) {
             // The leader expects the bytes of both CTAs; the peer's loads complete their
             // bytes on the leader's barrier (possibly before this expect, which is fine:
             // the phase cannot complete before the leader's single arrival).
             if (leader) ptx::mbar_arrive_expect_tx(full_local, CG * Sh::STAGE_BYTES);
-            auto ld2 = [&](uint32_t dst, const CUtensorMap* m, int c0, int c1) {
-              if (CG == 1) ptx::tma_load_2d(dst, m, full_c, c0, c1);
-              else ptx::tma_load_2d_pair(dst, m, full_c, c0, c1);
-            };
-            auto ld3 = [&](uint32_t dst, const CUtensorMap* m, int c0, int c1, int c2) {
-              if (CG == 1) ptx::tma_load_3d(dst, m, full_c, c0, c1, c2);
-              else ptx::tma_load_3d_pair(dst, m, full_c, c0, c1, c2);
-            };
-            if (MODE == kModeRows) {
-              const int k0 = kb * BK;
-              ld2(sa, &map_a, k0, ti.row0 + (int)rank * BMC);
-              const int nb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
-              if (!B_MN) {
-                ld3(sb, &map_b, k0, nb, ti.g);
-              } else {
-#pragma unroll
-                for (int j = 0; j < Sh::B_COLS / 64; ++j)
-                  ld3(sb + j * (BK * 128), &map_b, nb + j * 64, k0, ti.g);
-              }
+            const int k0 = kb * BK;
+            const int nb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+            if (CG == 1) ptx::tma_load_2d(sa, &map_a, full_c, k0, ti.row0);
+            else ptx::tma_load_2d_pair(sa, &map_a, full_c, k0, ti.row0 + (int)rank * BMC);
+            if (!B_MN) {
+              if (CG == 1) ptx::tma_load_3d(sb, &map_b, full_c, k0, nb, ti.g);
+              else ptx::tma_load_3d_pair(sb, &map_b, full_c, k0, nb, ti.g);
             } else {
-              const int pa = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
-              const int qb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
 #pragma unroll
-              for (int j = 0; j < BMC / 64; ++j) ld2(sa + j * (BK * 128), &map_a, pa + j * 64, r0);
-#pragma unroll
-              for (int j = 0; j < Sh::B_COLS / 64; ++j)
-                ld2(sb + j * (BK * 128), &map_b, qb + j * 64, r0);
+              for (int j = 0; j < Sh::B_COLS / 64; ++j) {
+                if (CG == 1) ptx::tma_load_3d(sb + j * (BK * 128), &map_b, full_c, nb + j * 64, k0, ti.g);
+                else ptx::tma_load_3d_pair(sb + j * (BK * 128), &map_b, full_c, nb + j * 64, k0, ti.g);
+              }
             }
-          }
-        } else {
-          // Masked wgrad block: load locally, zero the rows past the expert, hand over.
-          const uint32_t ab = ptx::smem_u32(&s.aux);
-          if (lane == 0) {
-            ptx::mbar_arrive_expect_tx(ab, Sh::STAGE_BYTES);
+          } else {
+            const int r0 = ti.row0 + kb * BK;
+            const bool masked = ti.row0 + ti.rows - r0 < BK;  // block reaches past the expert
             const int pa = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
             const int qb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+            if (!masked) {
+              if (leader) ptx::mbar_arrive_expect_tx(full_local, CG * Sh::STAGE_BYTES);
 #pragma unroll
-            for (int j = 0; j < BMC / 64; ++j)
-              ptx::tma_load_2d(sa + j * (BK * 128), &map_a, ab, pa + j * 64, r0);
+              for (int j = 0; j < BMC / 64; ++j) {
+                if (CG == 1) ptx::tma_load_2d(sa + j * (BK * 128), &map_a, full_c, pa + j * 64, r0);
+                else ptx::tma_load_2d_pair(sa + j * (BK * 128), &map_a, full_c, pa + j * 64, r0);
+              }
 #pragma unroll
-            for (int j = 0; j < Sh::B_COLS / 64; ++j)
-              ptx::tma_load_2d(sb + j * (BK * 128), &map_b, ab, qb + j * 64, r0);
+              for (int j = 0; j < Sh::B_COLS / 64; ++j) {
+                if (CG == 1) ptx::tma_load_2d(sb + j * (BK * 128), &map_b, full_c, qb + j * 64, r0);
+                else ptx::tma_load_2d_pair(sb + j * (BK * 128), &map_b, full_c, qb + j * 64, r0);
+              }
+            } else {
+              const uint32_t rb = ptx::smem_u32(&s.raw[stage]);
+              ptx::mbar_arrive_expect_tx(rb, Sh::STAGE_BYTES);
+#pragma unroll
+              for (int j = 0; j < BMC / 64; ++j)
+                ptx::tma_load_2d(sa + j * (BK * 128), &map_a, rb, pa + j * 64, r0);
+#pragma unroll
+              for (int j = 0; j < Sh::B_COLS / 64; ++j)
+                ptx::tma_load_2d(sb + j * (BK * 128), &map_b, rb, qb + j * 64, r0);
+            }
           }
-          __syncwarp();
-          const bool ok = ptx::wait_bounded(ab, aux_phase, abort_flag, kWaitTimeoutNs);
-          aux_phase ^= 1;
+        }
+        __syncwarp();
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (MODE == kModeWgrad && warp == 2) {
+    // ---------------------------------------------------------- masked-block fix-up
+    // Walks the same stage sequence as the producer.  For a block that reaches past the
+    // expert's last row: wait for its data on `raw`, zero the rows past the expert (a
+    // swizzled 128-byte row stays one row), fence the generic->async proxy, then hand the
+    // stage to the MMA (for a pair, the peer releases its rows to the leader first).
+    int stage = 0;
+    uint32_t raw_bits = 0, peer_bits = 0;  // per-stage parities
+    for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
+      const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
+      bool ok = true;
+      for (int kb = 0; kb < ti.nkb && ok; ++kb) {
+        const int r0 = ti.row0 + kb * BK;
+        const int valid = ti.row0 + ti.rows - r0;
+        if (valid < BK) {
+          const uint32_t rb = ptx::smem_u32(&s.raw[stage]);
+          ok = ptx::wait_bounded(rb, (raw_bits >> stage) & 1u, abort_flag, kWaitTimeoutNs);
+          raw_bits ^= 1u << stage;
           if (!ok) break;
           const int n16 = (BK - valid) * 8;  // 16-byte chunks to clear per 64-column box
           constexpr int kBoxes = (BMC + Sh::B_COLS) / 64;
@@ -371,24 +386,25 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           }
           ptx::fence_proxy_async_smem();
           __syncwarp();
+          const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
           if (CG == 1) {
             if (lane == 0) ptx::mbar_arrive(full_local);
           } else if (!leader) {
-            // Release the zeroed rows to the leader, which then arms `full` for both.
             if (lane == 0)
               ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&s.peer_done[stage]), 0));
           } else {
             const uint32_t pd = ptx::smem_u32(&s.peer_done[stage]);
-            const bool ok2 = ptx::wait_bounded_cluster(pd, (peer_phase_bits >> stage) & 1u,
-                                                       abort_flag, kWaitTimeoutNs);
-            peer_phase_bits ^= 1u << stage;
-            if (!ok2) break;
+            ok = ptx::wait_bounded_cluster(pd, (peer_bits >> stage) & 1u, abort_flag,
+                                           kWaitTimeoutNs);
+            peer_bits ^= 1u << stage;
+            if (!ok) break;
             if (lane == 0) ptx::mbar_arrive(full_local);
           }
+          __syncwarp();
         }
-        __syncwarp();
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == STAGES) stage = 0;
       }
+      if (!ok) break;
     }
   } else if (warp == 1 && leader) {
     // ---------------------------------------------------------- MMA issuer
@@ -462,6 +478,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     const int wr_row = lane;        // row written by this lane
     const int rd_chunk = lane & 3;  // 16-byte chunk read by this lane
     const int rd_row0 = lane >> 2;  // first row read by this lane (then +8, +16, +24)
+    const uint32_t cbuf_u32 = ptx::smem_u32(cbuf);
     int acc = 0;
     for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters, ++acc) {
       const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
@@ -472,16 +489,21 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const int n0 = ti.n_blk * BN;
       const int col_lo = h * (BN / 2);
       const int valid_cols = min(BN, p.n_out - n0);
-      int valid_rows;
+      int valid_rows, row_base;
       OutT* tile_ptr;  // element (0, 0) of this CTA's 128 rows of the tile
       if (MODE == kModeRows) {
         valid_rows = min(BMC, ti.rows - (int)rank * BMC);
-        tile_ptr = out + (int64_t)(ti.row0 + (int)rank * BMC) * p.n_out + n0;
+        row_base = ti.row0 + (int)rank * BMC;
+        tile_ptr = out + (int64_t)row_base * p.n_out + n0;
       } else {
-        const int prow = ti.m_blk * Sh::TILE_M + (int)rank * BMC;
-        valid_rows = min(BMC, p.p_out - prow);
-        tile_ptr = out + ((int64_t)ti.g * p.p_out + prow) * p.n_out + n0;
+        row_base = ti.m_blk * Sh::TILE_M + (int)rank * BMC;  // row inside expert g
+        valid_rows = min(BMC, p.p_out - row_base);
+        tile_ptr = out + ((int64_t)ti.g * p.p_out + row_base) * p.n_out + n0;
       }
+      // TMA stores clip at the output's edges, so they serve every wgrad tile and the
+      // row tiles whose 128 rows all belong to the expert; the others store with masks so
+      // they never touch the next expert's rows.
+      const bool use_tma = MODE == kModeWgrad || valid_rows == BMC;
 #if MOE_GMM_EPI_EXPERIMENT == 2
       const int nchunks = 0;
 #else
@@ -507,11 +529,26 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = 0u;
         }
+        // The previous TMA store from this buffer must have finished reading it.
+        if (lane == 0) ptx::bulk_wait_group_read<0>();
+        __syncwarp();
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int phys = i ^ ((wr_row >> 1) & 3);
           *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
               make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
+        }
+        if (use_tma) {
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int cx = n0 + col_lo + c * 32;
+            if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + q * 32);
+            else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + q * 32, ti.g);
+            ptx::bulk_commit_group();
+          }
+          if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
+          continue;
         }
         __syncwarp();
         const int col = col_lo + c * 32 + rd_chunk * 8;  // first column of this lane's chunk
@@ -540,6 +577,9 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         else ptx::mbar_arrive_relaxed_cluster(ptx::mapa_shared(eb, 0));
       }
     }
+    // The TMA stores must have landed before the CTA ends.
+    if (lane == 0) ptx::bulk_wait_group<0>();
+    __syncwarp();
   }
 
   // ------------------------------------------------------------ teardown

@@ -64,9 +64,10 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 16-bit element tensor map with 128-byte swizzle; dims/box innermost first.
+// 16-bit element tensor map (128-byte swizzle unless given); dims/box innermost first.
 static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, const uint64_t* dims,
-                    const uint32_t* box) {
+                    const uint32_t* box,
+                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t gdim[3], gstride[2];
@@ -81,7 +82,7 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, con
   const CUtensorMapDataType dt =
       dtype == MOE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(map, dt, (cuuint32_t)rank, const_cast<void*>(base), gdim, gstride, bdim, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rank=%d dims=%llu,%llu,%llu",
@@ -93,8 +94,8 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, con
 
 // ---------------------------------------------------------------- GEMM launchers
 template <int MODE, int CG, int FMT, bool A_MN, bool B_MN, typename OutT>
-static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const gmm::Params& p,
-                        cudaStream_t stream) {
+static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                        const gmm::Params& p, cudaStream_t stream) {
   auto kern = gmm::gmm_sm100_kernel<MODE, CG, FMT, A_MN, B_MN, OutT>;
   const int dev = current_device();
   static unsigned long long attr_set = 0;  // per-device bitmask, one per instantiation
@@ -132,7 +133,7 @@ static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const gmm:
   if (getenv("MOE_B200_DEBUG"))
     fprintf(stderr, "[moe_b200] gmm launch: mode=%d cg=%d grid=%d smem=%zu\n", MODE, CG, grid,
             gmm::smem_bytes<CG>());
-  MOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, p));
+  MOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p));
   MOE_LAUNCH_CHECK();
   return MOE_OK;
 }
@@ -147,12 +148,12 @@ static int pick_cg(int auto_cg) {
 
 template <int MODE, bool A_MN, bool B_MN>
 static int launch_fmt_cg(int dtype, int cg, const CUtensorMap& ma, const CUtensorMap& mb,
-                         const gmm::Params& p, cudaStream_t stream) {
+                         const CUtensorMap& mc, const gmm::Params& p, cudaStream_t stream) {
   if (dtype == MOE_BF16)
-    return cg == 2 ? launch_sm100<MODE, 2, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, p, stream)
-                   : launch_sm100<MODE, 1, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, p, stream);
-  return cg == 2 ? launch_sm100<MODE, 2, 0, A_MN, B_MN, __half>(ma, mb, p, stream)
-                 : launch_sm100<MODE, 1, 0, A_MN, B_MN, __half>(ma, mb, p, stream);
+    return cg == 2 ? launch_sm100<MODE, 2, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, mc, p, stream)
+                   : launch_sm100<MODE, 1, 1, A_MN, B_MN, __nv_bfloat16>(ma, mb, mc, p, stream);
+  return cg == 2 ? launch_sm100<MODE, 2, 0, A_MN, B_MN, __half>(ma, mb, mc, p, stream)
+                 : launch_sm100<MODE, 1, 0, A_MN, B_MN, __half>(ma, mb, mc, p, stream);
 }
 
 // Row mode (forward / dgrad): C[m_total, n_out] = A[m_total, k_red] . op(B[g]).
@@ -211,6 +212,13 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     int rc = make_map(&mb, B, dtype, 3, dims, box);
     if (rc) return rc;
   }
+  CUtensorMap mc;  // output, 32 x 32 boxes in the epilogue's 64-byte swizzle
+  {
+    const uint64_t dims[2] = {(uint64_t)n_out, (uint64_t)m_total};
+    const uint32_t box[2] = {32, 32};
+    int rc = make_map(&mc, C, dtype, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
   gmm::Params p;
   p.offsets = offsets;
   p.offsets_plus_one = plus_one;
@@ -220,8 +228,8 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   p.p_out = 0;
   p.k_red = (int)k_red;
   p.out = C;
-  return b_mn ? launch_fmt_cg<gmm::kModeRows, false, true>(dtype, cg, ma, mb, p, stream)
-              : launch_fmt_cg<gmm::kModeRows, false, false>(dtype, cg, ma, mb, p, stream);
+  return b_mn ? launch_fmt_cg<gmm::kModeRows, false, true>(dtype, cg, ma, mb, mc, p, stream)
+              : launch_fmt_cg<gmm::kModeRows, false, false>(dtype, cg, ma, mb, mc, p, stream);
 }
 
 // Wgrad mode: Out[g] [P, Q] = X[rows of g]^T . Y[rows of g]; X [m_total, P], Y [m_total, Q].
@@ -266,6 +274,13 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
     int rc = make_map(&my, Y, dtype, 2, dims, box);
     if (rc) return rc;
   }
+  CUtensorMap mo;  // output [E, P, Q], 32 x 32 boxes in the epilogue's 64-byte swizzle
+  {
+    const uint64_t dims[3] = {(uint64_t)Q, (uint64_t)P, (uint64_t)E};
+    const uint32_t box[3] = {32, 32, 1};
+    int rc = make_map(&mo, Out, dtype, 3, dims, box, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc) return rc;
+  }
   gmm::Params p;
   p.offsets = offsets;
   p.offsets_plus_one = plus_one;
@@ -275,7 +290,7 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
   p.p_out = (int)P;
   p.k_red = 0;
   p.out = Out;
-  return launch_fmt_cg<gmm::kModeWgrad, true, true>(dtype, cg, mx, my, p, stream);
+  return launch_fmt_cg<gmm::kModeWgrad, true, true>(dtype, cg, mx, my, mo, p, stream);
 }
 
 static int check_gmm_args(const void* a, const void* b, const void* c, const int32_t* offsets,
