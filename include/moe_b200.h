@@ -79,6 +79,21 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
                 void* permuted, int32_t* row_id_map, int32_t* offsets, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  moe_permute for callers that cannot allocate device
+ * memory at call time (work recorded into a stream capture or run from inside an
+ * allocator, runtimes that plan all memory ahead, fixed device arenas): the per-tile
+ * expert counts live in a 1 MiB array inside the library instead of in a workspace
+ * argument.  Same outputs and contract as moe_permute; the caller still passes inputs and
+ * outputs.  Sizes whose counts (ceil(T*K / 512) * E int32) exceed the array are rejected
+ * with MOE_ERR_INVALID_ARG; moe_permute_noalloc_max_slots(E) gives the largest T*K.
+ * The first call on a device looks up the array's device address (make it before any
+ * stream capture).  All calls share the one array: calls that overlap on the GPU (on
+ * different streams) race and must be serialised by the caller.  Calls no allocator. */
+int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                        int32_t topk, int64_t num_cols, int32_t num_experts, int64_t num_out,
+                        void* permuted, int32_t* row_id_map, int32_t* offsets, void* stream);
+size_t moe_permute_noalloc_max_slots(int32_t num_experts);
+
 /* ---------------------------------------------------------------- unpermute
  * Replaces tg::unpermute_forward (triton_gmm_ops/unpermute_ops.py:58-72, kernel :20-55).
  * out[t] = sum_k prob[t,k] * input[row_id_map[k*T+t]], accumulated in fp32 in k order

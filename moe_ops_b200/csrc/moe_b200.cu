@@ -547,4 +547,48 @@ int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t
   return gmm_wgrad(A, grad_C, grad_B, offsets, plus_one, m_total, k, n, E, dtype, s);
 }
 
+// ---------------------------------------------------------------- permute without allocation
+// For callers that cannot allocate device memory at call time: code running inside a
+// captured stream or a custom allocator's own callbacks, runtimes that pre-plan every
+// buffer, or hosts whose only device memory comes from a fixed arena.  The per-tile
+// expert counts that moe_permute keeps in caller-provided workspace live instead in this
+// file-scope array, which every GPU that loads the library holds until the process exits.
+static constexpr size_t kNoAllocScratchInts = 262144;  // 1 MiB: num_tiles * E counts
+static __device__ __align__(256) int32_t g_permute_scratch[kNoAllocScratchInts];
+static int32_t* g_permute_scratch_ptr[64] = {nullptr};  // device address, per device
+
+size_t moe_permute_noalloc_max_slots(int32_t E) {
+  if (E <= 0) return 0;
+  return (kNoAllocScratchInts / (size_t)E) * (size_t)kPermTile;
+}
+
+int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                        int32_t topk, int64_t num_cols, int32_t E, int64_t num_out,
+                        void* permuted, int32_t* row_id_map, int32_t* offsets, void* stream) {
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && E > 0,
+              "permute_noalloc: bad sizes T=%lld K=%d E=%d", (long long)num_tokens, topk, E);
+  const int64_t num_slots = num_tokens * topk;
+  const size_t need = (size_t)permute_num_tiles(num_slots) * (size_t)E;
+  if (need > kNoAllocScratchInts)
+    return set_error(MOE_ERR_INVALID_ARG,
+                     "permute_noalloc: T*K=%lld with E=%d needs %zu scratch counts, the fixed "
+                     "scratch holds %zu (at most %zu slots for this E); use moe_permute",
+                     (long long)num_slots, E, need, kNoAllocScratchInts,
+                     moe_permute_noalloc_max_slots(E));
+  const int dev = current_device();
+  MOE_REQUIRE(dev >= 0 && dev < 64, "permute_noalloc: device %d out of range", dev);
+  if (g_permute_scratch_ptr[dev] == nullptr) {
+    // One-time set-up on this device (the device is current): the host-side symbol is not
+    // a device address, so look the array's device address up.
+    void* ptr = nullptr;
+    MOE_CUDA_CHECK(cudaGetSymbolAddress(&ptr, g_permute_scratch));
+    g_permute_scratch_ptr[dev] = static_cast<int32_t*>(ptr);
+  }
+  // Every count the kernels read is written first by the histogram kernel of this call,
+  // so the array needs no clearing; calls that overlap on the GPU share it and race.
+  return moe_permute(input, dtype, indices, num_tokens, topk, num_cols, E, num_out, permuted,
+                     row_id_map, offsets, g_permute_scratch_ptr[dev],
+                     kNoAllocScratchInts * sizeof(int32_t), stream);
+}
+
 }  // extern "C"
