@@ -329,8 +329,88 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def _time_events(fn, steps, warmup):
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def run_case(args):
+    """Single-op cases (one GPU): per-op throughput and roofline fraction, and small
+    targets for ncu.  `gmm-*`: one grouped GEMM at cfg4 shapes (256 +- 16 rows per expert,
+    d=4096, H=11008) over --experts experts, or cfg2 (--cfg2).  `routing`: the cfg3
+    primitives (top-k, permute, unpermute fwd/bwd, permute_backward) on T=8192, d=4096."""
+    from moe_ops_b200 import _lib  # noqa: F401
+    import moe_ops_b200 as M
+    from moe_ops_b200.grouped_gemm_ops import gmm_bwd_B_raw, gmm_dgrad_raw, gmm_fwd_raw
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, kind = _peaks()
+    g = torch.Generator(device=dev).manual_seed(7)
+    res = {"case": args.case}
+    if args.case.startswith("gmm-"):
+        op = args.case[4:]
+        if args.cfg2:
+            E, K, N = 16, 4096, 4096
+            sizes = [1024] * 16
+        else:
+            E, K, N = args.experts, 4096, 11008
+            cpu_g = torch.Generator().manual_seed(0)
+            sizes = torch.bincount(torch.randint(0, E, (256 * E,), generator=cpu_g), minlength=E).tolist()
+        Mt = sum(sizes)
+        A = torch.randn(Mt, K, device=dev, generator=g).to(torch.bfloat16)
+        B = (torch.randn(E, N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        gC = torch.randn(Mt, N, device=dev, generator=g).to(torch.bfloat16)
+        off = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        off[1:] = torch.tensor(sizes, device=dev).cumsum(0).to(torch.int32)
+        fn = {"fwd": lambda: gmm_fwd_raw(A, B, off, True),
+              "dgrad": lambda: gmm_dgrad_raw(gC, B, off, True),
+              "wgrad": lambda: gmm_bwd_B_raw(A, B, off, gC, True)}[op]
+        ms = _time_events(fn, args.steps, args.warmup)
+        tf = 2.0 * Mt * N * K / (ms * 1e-3) / 1e12
+        res.update({"config": {"E": E, "rows": Mt, "K": K, "N": N, "cfg2": bool(args.cfg2)},
+                    "ms": round(ms, 4), "tflops": round(tf, 1),
+                    "frac_of_burst_peak": round(tf / peaks["bf16_tflops"], 4),
+                    "peak_kind": kind})
+    elif args.case == "routing":
+        T, d, E, K = 8192, 4096, 64, 2
+        x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+        logits = torch.randn(T, E, device=dev, generator=g)
+        w, idx = M.fused_topk_softmax(logits, K)
+        perm, rid, off = M.permute(x, idx, E=E)
+        prob = w.float()
+        gout = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+        row = T * d * 2
+        cases = {
+            "topk_fwd": (lambda: M.fused_topk_softmax(logits, K), T * E * 4 + T * K * 8),
+            "permute": (lambda: M.permute(x, idx, E=E), row * (1 + K) + T * K * 12),
+            "unpermute_fwd": (lambda: M.unpermute_forward(perm, rid, prob, T, K), row * (1 + K)),
+            "permute_backward": (lambda: M.permute_backward(perm, rid, T, K), row * (1 + K)),
+            "unpermute_bwd": (lambda: M.unpermute_backward(gout, perm, rid, prob, T, K), row * (1 + 2 * K)),
+        }
+        for name, (fn, nbytes) in cases.items():
+            ms = _time_events(fn, args.steps, args.warmup)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                         "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}
+        res["peak_kind"] = kind
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="layer",
+                    help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing")
+    ap.add_argument("--experts", type=int, default=64, help="gmm-* cases: experts (cfg4 shapes)")
+    ap.add_argument("--cfg2", action="store_true", help="gmm-* cases: BASELINE config 2 shapes")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -339,6 +419,8 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.case != "layer":
+        run_case(args)
     else:
         run_ours(args)
 
