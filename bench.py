@@ -10,8 +10,9 @@ unpermute, then the full backward (6 grouped GEMMs, unpermute/permute/top-k back
 
 `value` is grouped-GEMM TFLOP/s of the whole job (9 GEMMs per step, 2*T*K*d*H FLOPs each).
 Inputs (17.3 GB of weights) are far larger than L2, so no flush is needed between steps.
-Under torchrun (N > 1) every rank runs the same single-GPU layer on its own tokens
-(weak scaling); the expert-parallel path lives in moe_ops_b200.ep.
+Under torchrun (N > 1) the layer is expert-parallel (moe_ops_b200.ep): each rank holds
+E/N experts and its own 8192 tokens, tokens go to their experts' ranks and back through
+NCCL all-to-alls (weak scaling: per-rank work is fixed as N grows).
 
 `--impl reference` times the reference's PyTorch-native CPU path (restated in oracle/)
 on the host cores, on a bounded sample of the same workload (8 of the 64 experts with
@@ -144,8 +145,19 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     T, d, E, K, H = CFG["tokens"], CFG["d_model"], CFG["experts"], CFG["top_k"], CFG["hidden"]
 
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    layer = MoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16).init_normal(0.02, gen)
+    if world == 1:
+        gen = torch.Generator(device=dev).manual_seed(1234)
+        layer = MoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16).init_normal(0.02, gen)
+    else:
+        # Expert parallelism: this rank holds E/world experts, the router is replicated.
+        from moe_ops_b200.ep import EPMoELayer
+
+        layer = EPMoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16)
+        with torch.no_grad():
+            layer.w_router.normal_(0.0, 0.02, generator=torch.Generator(device=dev).manual_seed(1234))
+            gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+            for w in (layer.w_gate, layer.w_up, layer.w_down):
+                w.normal_(0.0, 0.02, generator=gen)
     x, grad_out = _make_inputs(dev, T, 99 + rank)
     flops_step = layer_gemm_flops(T, K, d, H)
 
@@ -237,7 +249,8 @@ def run_ours(args):
         "config": {
             "workload": "cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16",
             "model": "moe_layer_swiglu", "global_batch": T * world, "seq_len": 1,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "tokens_per_rank": T,
             "l2": "inputs larger than L2 (17.3 GB expert weights), no flush",
             "gemm_flops_per_step": flops_step,
         },

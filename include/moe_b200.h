@@ -79,6 +79,13 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
                 void* permuted, int32_t* row_id_map, int32_t* offsets, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* Copy step of moe_permute with a caller-supplied map: out[row_id_map[k*T+t]] = input[t]
+ * for every k (input [T, C], out rows as many as the map names).  This is the copy of the
+ * reference's permute scatter (permute_ops.py:50-74) without the counting sort; it is also
+ * the backward of permute_backward with K = 1. */
+int moe_scatter_rows(const void* input, int dtype, const int32_t* row_id_map, int64_t num_tokens,
+                     int32_t topk, int64_t num_cols, void* out, void* stream);
+
 /* No counterpart in the reference.  moe_permute for callers that cannot allocate device
  * memory at call time (work recorded into a stream capture or run from inside an
  * allocator, runtimes that plan all memory ahead, fixed device arenas): the per-tile

@@ -424,6 +424,31 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   return MOE_OK;
 }
 
+int moe_scatter_rows(const void* input, int dtype, const int32_t* row_id_map, int64_t num_tokens,
+                     int32_t topk, int64_t num_cols, void* out, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "scatter_rows: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "scatter_rows: bad sizes");
+  if (num_tokens == 0 || num_cols == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0 && aligned16(input) && aligned16(out);
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+#define MOE_SC(TT)                                                                                   \
+  if (vec)                                                                                          \
+    permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>(                                   \
+        (const TT*)input, row_id_map, (TT*)out, num_tokens, topk, num_cols);                       \
+  else                                                                                              \
+    permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>(                                  \
+        (const TT*)input, row_id_map, (TT*)out, num_tokens, topk, num_cols);
+  switch (dtype) {
+    case MOE_F32: MOE_SC(float) break;
+    case MOE_F16: MOE_SC(__half) break;
+    default: MOE_SC(__nv_bfloat16) break;
+  }
+#undef MOE_SC
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
 int moe_unpermute_fwd(const void* input, int dtype, const int32_t* row_id_map, const void* prob,
                       int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols, void* out,
                       void* stream) {

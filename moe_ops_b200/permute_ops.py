@@ -101,3 +101,50 @@ class PermuteAutograd(torch.autograd.Function):
 def permute(input, indices, num_out_tokens=0, E=None):
     """Differentiable counting-sort permute."""
     return PermuteAutograd.apply(input, indices, num_out_tokens, E)
+
+
+# ---------------------------------------------------------------- rows through a given map
+
+
+@torch.library.custom_op(f"{_NS}::scatter_rows", mutates_args=())
+def scatter_rows(input: torch.Tensor, row_id_map: torch.Tensor, num_out: int,
+                 topK: int) -> torch.Tensor:
+    """out[row_id_map[k*T+t]] = input[t] for every k: the copy step of permute with a given
+    map (rows the map does not name are left unwritten)."""
+    _lib.require_cuda(input, row_id_map)
+    input = input.contiguous()
+    row_id_map = row_id_map.to(torch.int32).contiguous()
+    T, C = input.shape
+    out = torch.empty(num_out, C, device=input.device, dtype=input.dtype)
+    with torch.cuda.device(input.device):
+        st = _lib.load().moe_scatter_rows(_lib.ptr(input), _lib.dtype_code(input.dtype),
+                                          _lib.ptr(row_id_map), T, topK, C, _lib.ptr(out),
+                                          _lib.stream_of(input))
+    _lib.check(st, "moe_scatter_rows")
+    _lib.count_launches(1)
+    return out
+
+
+@scatter_rows.register_fake
+def _(input, row_id_map, num_out, topK):
+    return torch.empty(num_out, input.shape[1], device=input.device, dtype=input.dtype)
+
+
+class GatherRows(torch.autograd.Function):
+    """rows -> token order through a one-to-one map (K = 1): out[t] = rows[row_id_map[t]].
+    Forward is permute_backward (exact for K = 1), backward the matching scatter."""
+
+    @staticmethod
+    def forward(ctx, rows, row_id_map):
+        ctx.save_for_backward(row_id_map)
+        ctx.n = rows.shape[0]
+        return permute_backward(rows, row_id_map, row_id_map.numel(), 1)
+
+    @staticmethod
+    def backward(ctx, g):
+        (row_id_map,) = ctx.saved_tensors
+        return torch.ops.moeb200.scatter_rows(g, row_id_map, ctx.n, 1), None
+
+
+def gather_rows(rows, row_id_map):
+    return GatherRows.apply(rows, row_id_map)
