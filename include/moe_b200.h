@@ -79,6 +79,14 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
                 void* permuted, int32_t* row_id_map, int32_t* offsets, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* SwiGLU between the expert GEMMs: out = silu(gate) * up over n elements, replacing the
+ * reference layer's `F.silu(gate) * up` (tests/test_moe.py:82) and its autograd backward.
+ * Rounding follows those PyTorch passes: silu rounded to dtype, then the product. */
+int moe_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream);
+/* grad_gate = silu'(gate) * rnd(grad_out * up), grad_up = grad_out * rnd(silu(gate)). */
+int moe_swiglu_bwd(const void* grad_out, const void* gate, const void* up, void* grad_gate,
+                   void* grad_up, int64_t n, int dtype, void* stream);
+
 /* Copy step of moe_permute with a caller-supplied map: out[row_id_map[k*T+t]] = input[t]
  * for every k (input [T, C], out rows as many as the map names).  This is the copy of the
  * reference's permute scatter (permute_ops.py:50-74) without the counting sort; it is also

@@ -37,6 +37,8 @@ SIGNATURES = {
     "moe_permute_noalloc": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32,
                                      _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr]),
     "moe_permute_noalloc_max_slots": (_c_size, [_c_i32]),
+    "moe_swiglu_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
+    "moe_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_int, _c_ptr]),
     "moe_scatter_rows": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_ptr, _c_ptr]),
     "moe_unpermute_fwd": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_ptr, _c_int, _c_i64, _c_i32, _c_i64,
                                    _c_ptr, _c_ptr]),

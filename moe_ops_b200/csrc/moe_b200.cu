@@ -14,6 +14,7 @@
 #include "gmm_simt.cuh"
 #include "gmm_sm100.cuh"
 #include "permute.cuh"
+#include "swiglu.cuh"
 #include "topk_softmax.cuh"
 
 namespace moe {
@@ -420,6 +421,47 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
     default: MOE_COPY(__nv_bfloat16) break;
   }
 #undef MOE_COPY
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+static unsigned elementwise_grid(int64_t n, int per_thread) {
+  const int64_t blocks = (n / per_thread + 255) / 256;
+  const int64_t cap = (int64_t)num_sms(current_device()) * 8;
+  return (unsigned)std::max<int64_t>(1, std::min(blocks, cap));
+}
+
+int moe_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream) {
+  MOE_REQUIRE(dtype == MOE_BF16 || dtype == MOE_F16 || dtype == MOE_F32, "swiglu: bad dtype %d", dtype);
+  MOE_REQUIRE(n >= 0, "swiglu: negative size");
+  MOE_REQUIRE(aligned16(gate) && aligned16(up) && aligned16(out), "swiglu: pointers must be 16-byte aligned");
+  if (n == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned grid = elementwise_grid(n, 16 / dtype_size(dtype));
+  switch (dtype) {
+    case MOE_F32: swiglu_fwd_kernel<float><<<grid, 256, 0, s>>>((const float*)gate, (const float*)up, (float*)out, n); break;
+    case MOE_F16: swiglu_fwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)gate, (const __half*)up, (__half*)out, n); break;
+    default: swiglu_fwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)gate, (const __nv_bfloat16*)up, (__nv_bfloat16*)out, n);
+  }
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_swiglu_bwd(const void* grad_out, const void* gate, const void* up, void* grad_gate,
+                   void* grad_up, int64_t n, int dtype, void* stream) {
+  MOE_REQUIRE(dtype == MOE_BF16 || dtype == MOE_F16 || dtype == MOE_F32, "swiglu_bwd: bad dtype %d", dtype);
+  MOE_REQUIRE(n >= 0, "swiglu_bwd: negative size");
+  MOE_REQUIRE(aligned16(grad_out) && aligned16(gate) && aligned16(up) && aligned16(grad_gate) &&
+                  aligned16(grad_up),
+              "swiglu_bwd: pointers must be 16-byte aligned");
+  if (n == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const unsigned grid = elementwise_grid(n, 16 / dtype_size(dtype));
+  switch (dtype) {
+    case MOE_F32: swiglu_bwd_kernel<float><<<grid, 256, 0, s>>>((const float*)grad_out, (const float*)gate, (const float*)up, (float*)grad_gate, (float*)grad_up, n); break;
+    case MOE_F16: swiglu_bwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)grad_out, (const __half*)gate, (const __half*)up, (__half*)grad_gate, (__half*)grad_up, n); break;
+    default: swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)grad_out, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)up, (__nv_bfloat16*)grad_gate, (__nv_bfloat16*)grad_up, n);
+  }
   MOE_LAUNCH_CHECK();
   return MOE_OK;
 }

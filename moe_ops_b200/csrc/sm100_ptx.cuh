@@ -6,6 +6,10 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#ifndef MOE_WAIT_CHECK_MASK
+#define MOE_WAIT_CHECK_MASK 1023u  // poll the abort flag / clock every 1024 try_waits
+#endif
+
 namespace moe {
 namespace ptx {
 
@@ -53,7 +57,7 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, vola
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 0) {
+    if ((it & MOE_WAIT_CHECK_MASK) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > timeout_ns) {
         *abort = 1;
@@ -105,7 +109,7 @@ __device__ __forceinline__ bool wait_bounded_cluster(uint32_t bar, uint32_t pari
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 15u) == 0) {
+    if ((it & MOE_WAIT_CHECK_MASK) == 0) {
       if (*abort) return false;
       if (globaltimer() - t0 > timeout_ns) {
         *abort = 1;

@@ -41,11 +41,13 @@ class EPOps:
     permute: Callable       # (x, indices [T,K], E) -> (permuted, row_id_map, offsets[E+1])
     unpermute: Callable     # (rows, row_id_map, prob | None (K=1 gather), T, K) -> out [T, d]
     grouped_gemm: Callable  # (A, B [E,N,K], offsets) -> C
+    swiglu: Callable = None  # (gate, up) -> silu(gate) * up; None = PyTorch elementwise
 
 
 def cuda_ops() -> EPOps:
     from . import fused_topk_softmax, grouped_gemm, permute, unpermute
     from .permute_ops import gather_rows
+    from .swiglu_ops import swiglu
 
     def _unpermute(rows, rid, prob, T, K):
         if prob is None:
@@ -56,7 +58,8 @@ def cuda_ops() -> EPOps:
     return EPOps(topk=lambda lg, K: fused_topk_softmax(lg, K),
                  permute=lambda x, idx, E: permute(x, idx, E=E),
                  unpermute=_unpermute,
-                 grouped_gemm=lambda a, b, off: grouped_gemm(a, b, off, True))
+                 grouped_gemm=lambda a, b, off: grouped_gemm(a, b, off, True),
+                 swiglu=swiglu)
 
 
 # ------------------------------------------------------------------ index bookkeeping
@@ -139,7 +142,8 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
     grouped, rid2, off2 = ops.permute(recv, ids.unsqueeze(1), el)
     gate = ops.grouped_gemm(grouped, w_gate_local, off2)
     up = ops.grouped_gemm(grouped, w_up_local, off2)
-    down = ops.grouped_gemm(F.silu(gate) * up, w_down_local, off2)
+    h = ops.swiglu(gate, up) if ops.swiglu is not None else F.silu(gate) * up
+    down = ops.grouped_gemm(h, w_down_local, off2)
     back = ops.unpermute(down, rid2, None, n_recv, 1)
     home = all_to_all_rows(back, recv_sizes, send_sizes, group)
     return ops.unpermute(home, rid, weights, T, top_k)

@@ -7,7 +7,7 @@ Same structure as the reference's example layer SingleGpuMoE (tests/test_moe.py:
     perm, row_id_map, offsets = permute(x, idx, E=E)
     gate    = grouped_gemm(perm, w_gate, offsets)     [T*K, H]
     up      = grouped_gemm(perm, w_up, offsets)       [T*K, H]
-    h       = silu(gate) * up                         (torch elementwise)
+    h       = silu(gate) * up                         (fused SwiGLU kernel)
     down    = grouped_gemm(h, w_down, offsets)        [T*K, d]
     out     = unpermute(down, row_id_map, w, T, K)
 
@@ -16,11 +16,11 @@ Weights: w_router [E, d], w_gate / w_up [E, H, d], w_down [E, d, H] (trans_b=Tru
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from .fused_topk_softmax_ops import fused_topk_softmax
 from .grouped_gemm_ops import grouped_gemm
 from .permute_ops import permute
+from .swiglu_ops import swiglu
 from .unpermute_ops import unpermute
 
 
@@ -34,7 +34,7 @@ def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Ten
     permuted, row_id_map, offsets = permute(x, indices, E=E)
     gate = grouped_gemm(permuted, w_gate, offsets, trans_b=True)
     up = grouped_gemm(permuted, w_up, offsets, trans_b=True)
-    h = F.silu(gate) * up
+    h = swiglu(gate, up)
     down = grouped_gemm(h, w_down, offsets, trans_b=True)
     return unpermute(down, row_id_map, weights, num_tokens, top_k)
 
