@@ -377,7 +377,8 @@ def run_case(args):
         else:
             E, K, N = args.experts, 4096, 11008
             cpu_g = torch.Generator().manual_seed(0)
-            sizes = torch.bincount(torch.randint(0, E, (256 * E,), generator=cpu_g), minlength=E).tolist()
+            sizes = torch.bincount(torch.randint(0, E, (args.rows_per_expert * E,), generator=cpu_g),
+                                   minlength=E).tolist()
         Mt = sum(sizes)
         A = torch.randn(Mt, K, device=dev, generator=g).to(torch.bfloat16)
         B = (torch.randn(E, N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
@@ -424,6 +425,7 @@ def main():
                     help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing")
     ap.add_argument("--experts", type=int, default=64, help="gmm-* cases: experts (cfg4 shapes)")
     ap.add_argument("--cfg2", action="store_true", help="gmm-* cases: BASELINE config 2 shapes")
+    ap.add_argument("--rows-per-expert", type=int, default=256, help="gmm-* cases: mean rows")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
