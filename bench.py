@@ -411,7 +411,15 @@ def run_case(args):
             "unpermute_bwd": (lambda: M.unpermute_backward(gout, perm, rid, prob, T, K), row * (1 + 2 * K)),
         }
         for name, (fn, nbytes) in cases.items():
-            ms = _time_events(fn, args.steps, args.warmup)
+            # Captured in a CUDA graph and replayed: GPU time only (eager timing of these
+            # short ops would measure the Python/launch path instead).
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            ms = _time_events(graph.replay, args.steps, args.warmup)
             gbs = nbytes / (ms * 1e-3) / 1e9
             res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
                          "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}

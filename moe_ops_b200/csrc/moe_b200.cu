@@ -306,14 +306,17 @@ static int check_gmm_args(const void* a, const void* b, const void* c, const int
 }
 
 // ---------------------------------------------------------------- permute workspace
+// Workspace: cnt[E][num_tiles] int32.
 struct PermuteWorkspace {
   int64_t num_tiles;
   size_t cnt_bytes;
+  size_t total_bytes;
 };
 static PermuteWorkspace permute_ws(int64_t T, int K, int E) {
   PermuteWorkspace w;
   w.num_tiles = permute_num_tiles(T * (int64_t)K);
   w.cnt_bytes = (size_t)w.num_tiles * E * sizeof(int32_t);
+  w.total_bytes = w.cnt_bytes + 16;
   return w;
 }
 
@@ -365,7 +368,7 @@ int moe_topk_softmax_bwd(const void* grad_weights, const void* weights, const in
 
 size_t moe_permute_workspace_bytes(int64_t num_tokens, int32_t topk, int32_t E) {
   if (num_tokens <= 0 || topk <= 0 || E <= 0) return 16;
-  return permute_ws(num_tokens, topk, E).cnt_bytes + 16;
+  return permute_ws(num_tokens, topk, E).total_bytes;
 }
 
 int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
@@ -386,23 +389,21 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
     return MOE_OK;
   }
   const PermuteWorkspace w = permute_ws(num_tokens, topk, E);
-  if (workspace == nullptr || workspace_bytes < w.cnt_bytes)
-    return set_error(MOE_ERR_WORKSPACE, "permute: workspace needs %zu bytes (got %zu)", w.cnt_bytes,
-                     workspace_bytes);
+  if (workspace == nullptr || workspace_bytes < w.total_bytes)
+    return set_error(MOE_ERR_WORKSPACE, "permute: workspace needs %zu bytes (got %zu)",
+                     w.total_bytes, workspace_bytes);
   int32_t* cnt = static_cast<int32_t*>(workspace);
   const unsigned tiles = (unsigned)w.num_tiles;
   permute_hist_kernel<<<tiles, kPermTile, E * sizeof(int32_t), s>>>(indices, num_slots, E, cnt,
                                                                      w.num_tiles);
   MOE_LAUNCH_CHECK();
-  permute_scan_kernel<<<1, kScanThreads, 0, s>>>(cnt, w.num_tiles, E, offsets);
-  MOE_LAUNCH_CHECK();
-  const size_t rank_smem = (size_t)kPermTileWarps * E * sizeof(int32_t);
+  const size_t rank_smem = (size_t)(kPermTileWarps + 2) * E * sizeof(int32_t);
   if (rank_smem > 48 * 1024) {
     MOE_CUDA_CHECK(cudaFuncSetAttribute(permute_rank_kernel,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rank_smem));
   }
   permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
-                                                          cnt, w.num_tiles, row_id_map);
+                                                          cnt, w.num_tiles, row_id_map, offsets);
   MOE_LAUNCH_CHECK();
   if (num_cols == 0) return MOE_OK;
   const int es = dtype_size(dtype);

@@ -11,12 +11,12 @@
 // expert group is whatever the GPU scheduler produced.  Here the order is fixed: slot
 // j = t*K + k goes to  offsets[e] + #{ j' < j : expert(j') = e },  i.e. the order of a
 // stable argsort of the flattened indices (the reference's own PyTorch oracle,
-// tests/test_permute.py:16-37).  Four launches:
-//   1. permute_hist_kernel   per-tile expert histogram  -> cnt[e][tile]
-//   2. permute_scan_kernel   one block: exclusive scan of cnt in (e, tile) order, offsets
-//   3. permute_rank_kernel   per-tile stable rank (warp match + per-warp column scan)
-//                            -> row_id_map
-//   4. permute_copy_kernel   token-major row copy: read input[t] once, write its K rows
+// tests/test_permute.py:16-37).  Three launches:
+//   1. permute_hist_kernel   per-tile expert histogram -> cnt[e][tile]
+//   2. permute_rank_kernel   per tile: its bases from the whole (small) count matrix, the
+//                            offsets (block 0), then the stable rank (warp match + per-warp
+//                            column scan) -> row_id_map
+//   3. permute_copy_kernel   token-major row copy: read input[t] once, write its K rows
 //                            with 16-byte vector stores.
 #pragma once
 
@@ -49,49 +49,61 @@ permute_hist_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int E,
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[(int64_t)e * num_tiles + blockIdx.x] = s_hist[e];
 }
 
-// ---------------------------------------------------------------- 2. scan (single block)
-// In place: cnt[e][tile] becomes the first destination row of expert e's slots in that
-// tile; offsets[e] = first row of expert e, offsets[E] = number of valid slots.
-constexpr int kScanThreads = 1024;
-__global__ void __launch_bounds__(kScanThreads)
-permute_scan_kernel(int32_t* __restrict__ cnt, int64_t num_tiles, int E,
-                    int32_t* __restrict__ offsets) {
-  __shared__ int32_t s_part[kScanThreads];
-  const int64_t n = num_tiles * E;
-  const int64_t chunk = (n + kScanThreads - 1) / kScanThreads;
-  const int64_t lo = threadIdx.x * chunk;
-  const int64_t hi = lo + chunk < n ? lo + chunk : n;
-  int32_t sum = 0;
-  for (int64_t i = lo; i < hi; ++i) sum += cnt[i];
-  s_part[threadIdx.x] = sum;
-  __syncthreads();
-  // Hillis-Steele inclusive scan of the per-thread sums.
-  for (int off = 1; off < kScanThreads; off <<= 1) {
-    const int32_t v = threadIdx.x >= off ? s_part[threadIdx.x - off] : 0;
-    __syncthreads();
-    s_part[threadIdx.x] += v;
-    __syncthreads();
-  }
-  int32_t run = s_part[threadIdx.x] - sum;  // exclusive prefix of this chunk
-  for (int64_t i = lo; i < hi; ++i) {
-    const int32_t c = cnt[i];
-    cnt[i] = run;
-    if (i % num_tiles == 0) offsets[i / num_tiles] = run;
-    run += c;
-  }
-  if (threadIdx.x == kScanThreads - 1) offsets[E] = s_part[kScanThreads - 1];
-}
-
-// ---------------------------------------------------------------- 3. stable rank
+// ---------------------------------------------------------------- 2. bases + stable rank
+// Each block derives what it needs from the whole count matrix cnt[E][num_tiles] (small,
+// L2-resident), so no separate scan launch is needed:
+//   base[e] = offsets[e] + sum_{t < tile} cnt[e][t],  offsets[e] = sum_{e' < e, all t} cnt.
+// Block 0 also writes offsets[E+1].  Then the tile's slots are ranked stably: warp match for
+// the rank inside a warp, a per-warp column scan across the warps of the tile.
+// Dynamic shared memory: (kPermTileWarps + 2) * E int32.
 __global__ void __launch_bounds__(kPermTile)
 permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t num_tokens,
-                    int K, int E, const int32_t* __restrict__ base, int64_t num_tiles,
-                    int32_t* __restrict__ row_id_map) {
-  extern __shared__ int32_t s_cnt[];  // [kPermTileWarps][E]
+                    int K, int E, const int32_t* __restrict__ cnt, int64_t num_tiles,
+                    int32_t* __restrict__ row_id_map, int32_t* __restrict__ offsets) {
+  extern __shared__ int32_t s_cnt[];     // [kPermTileWarps][E]
+  int32_t* s_before = s_cnt + kPermTileWarps * E;  // [E] this expert's rows in earlier tiles
+  int32_t* s_total = s_before + E;                 // [E] this expert's rows in all tiles
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tile = blockIdx.x;
   for (int i = threadIdx.x; i < kPermTileWarps * E; i += blockDim.x) s_cnt[i] = 0;
+  // Per-expert sums over the tiles (a warp per expert, lanes over tiles).
+  for (int x = warp; x < E; x += kPermTileWarps) {
+    int32_t before = 0, total = 0;
+    for (int64_t t = lane; t < num_tiles; t += 32) {
+      const int32_t c = cnt[(int64_t)x * num_tiles + t];
+      total += c;
+      if (t < tile) before += c;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      before += __shfl_xor_sync(0xffffffffu, before, off);
+      total += __shfl_xor_sync(0xffffffffu, total, off);
+    }
+    if (lane == 0) { s_before[x] = before; s_total[x] = total; }
+  }
   __syncthreads();
-  const int64_t j = (int64_t)blockIdx.x * kPermTile + threadIdx.x;
+  // Exclusive prefix of the totals over experts (one warp; E <= kMaxExperts).
+  if (warp == 0) {
+    int32_t carry = 0;
+    for (int x0 = 0; x0 < E; x0 += 32) {
+      const int x = x0 + lane;
+      const int32_t v = x < E ? s_total[x] : 0;
+      int32_t inc = v;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int32_t o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
+      }
+      if (x < E) {
+        const int32_t first = carry + inc - v;  // offsets[x]
+        if (tile == 0) offsets[x] = first;
+        s_before[x] += first;
+      }
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (tile == 0 && lane == 0) offsets[E] = carry;
+  }
+  const int64_t j = tile * kPermTile + threadIdx.x;
   int e = -1;
   if (j < num_slots) {
     e = flat[j];
@@ -99,11 +111,11 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
   }
   const unsigned peers = __match_any_sync(0xffffffffu, e);
   const int intra = __popc(peers & ((1u << lane) - 1u));
+  __syncthreads();
   if (e >= 0 && intra == 0) s_cnt[warp * E + e] = __popc(peers);
   __syncthreads();
-  // Column scan over the warps of this tile, seeded with the tile's global base.
   for (int x = threadIdx.x; x < E; x += blockDim.x) {
-    int32_t run = base[(int64_t)x * num_tiles + blockIdx.x];
+    int32_t run = s_before[x];
 #pragma unroll
     for (int w = 0; w < kPermTileWarps; ++w) {
       const int32_t c = s_cnt[w * E + x];
@@ -312,26 +324,44 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
     p_k[k] = __shfl_sync(0xffffffffu, p_lane, k);
   }
   if constexpr (VEC) {
+    // U 16-byte chunks per lane and iteration: all their loads are issued before use.
     constexpr int NV = Vec16<T>::N;
+    constexpr int U = 2;
     const int64_t nv = num_cols / NV;
-    for (int64_t c = lane; c < nv; c += 32) {
-      float g[NV];
-      unpack16<T>(ld_stream(reinterpret_cast<const uint4*>(g_row) + c), g);
+    for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
+      uint4 graw[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t c = c0 + u * 32 + lane;
+        if (c < nv) graw[u] = ld_stream(reinterpret_cast<const uint4*>(g_row) + c);
+      }
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k >= K) break;
         const int32_t s = src_k[k];
         const float p = p_k[k];
         if (s < 0) continue;
-        float v[NV];
-        unpack16<T>(ld_stream(reinterpret_cast<const uint4*>(input + (int64_t)s * num_cols) + c), v);
-        float ag[NV];
+        const uint4* in4 = reinterpret_cast<const uint4*>(input + (int64_t)s * num_cols);
+        uint4 vraw[U];
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          dot[k] = fmaf(g[i], v[i], dot[k]);
-          ag[i] = __fmul_rn(g[i], p);
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + u * 32 + lane;
+          if (c < nv) vraw[u] = ld_stream(in4 + c);
         }
-        reinterpret_cast<uint4*>(act_grad + (int64_t)s * num_cols)[c] = pack16<T>(ag);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + u * 32 + lane;
+          if (c >= nv) continue;
+          float g[NV], v[NV], ag[NV];
+          unpack16<T>(graw[u], g);
+          unpack16<T>(vraw[u], v);
+#pragma unroll
+          for (int i = 0; i < NV; ++i) {
+            dot[k] = fmaf(g[i], v[i], dot[k]);
+            ag[i] = __fmul_rn(g[i], p);
+          }
+          reinterpret_cast<uint4*>(act_grad + (int64_t)s * num_cols)[c] = pack16<T>(ag);
+        }
       }
     }
   } else {
