@@ -32,7 +32,19 @@ import torch
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-CFG = dict(tokens=8192, d_model=4096, experts=64, top_k=2, hidden=11008)
+CONFIGS = {
+    # BASELINE config 4 (the headline): every rank holds 8192 tokens (weak scaling).
+    "cfg4": dict(tokens=8192, d_model=4096, experts=64, top_k=2, hidden=11008, fp32_routing=False,
+                 zipf=False, global_tokens=False, router_std=0.02,
+                 workload="cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16"),
+    # 32768 tokens in total split over the ranks (strong scaling), router
+    # logits ~ N(0, 1) plus a Zipf bias 1.5*log(1/rank^1.2) over a random expert order.
+    "cfg5": dict(tokens=32768, d_model=7168, experts=256, top_k=8, hidden=2048, fp32_routing=True,
+                 zipf=True, global_tokens=True, router_std=None,
+                 workload="cfg5 skewed SwiGLU MoE fwd+bwd, T=32768 d=7168 E=256 topK=8 H=2048 bf16, "
+                          "fp32 routing, Zipf(1.2) router bias"),
+}
+CFG = CONFIGS["cfg4"]
 METRIC = "moe_layer_fwd_bwd_grouped_gemm_tflops"
 
 
@@ -125,10 +137,10 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def _make_inputs(dev, T, seed):
+def _make_inputs(dev, T, d, seed):
     g = torch.Generator(device=dev).manual_seed(seed)
-    x = torch.randn(T, CFG["d_model"], device=dev, generator=g).to(torch.bfloat16)
-    go = torch.randn(T, CFG["d_model"], device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+    go = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
     return x, go
 
 
@@ -143,22 +155,37 @@ def run_ours(args):
         dist.init_process_group("nccl")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    T, d, E, K, H = CFG["tokens"], CFG["d_model"], CFG["experts"], CFG["top_k"], CFG["hidden"]
+    cfg = CONFIGS[args.config]
+    d, E, K, H = cfg["d_model"], cfg["experts"], cfg["top_k"], cfg["hidden"]
+    T = cfg["tokens"] // world if cfg["global_tokens"] else cfg["tokens"]
+    router_std = cfg["router_std"] or d ** -0.5  # None: logits ~ N(0, 1)
 
     if world == 1:
+        layer = MoELayer(d, E, K, H, fp32_routing=cfg["fp32_routing"], device=dev,
+                         dtype=torch.bfloat16)
         gen = torch.Generator(device=dev).manual_seed(1234)
-        layer = MoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16).init_normal(0.02, gen)
+        with torch.no_grad():
+            for w in (layer.w_gate, layer.w_up, layer.w_down):
+                w.normal_(0.0, 0.02, generator=gen)
     else:
         # Expert parallelism: this rank holds E/world experts, the router is replicated.
         from moe_ops_b200.ep import EPMoELayer
 
-        layer = EPMoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16)
+        layer = EPMoELayer(d, E, K, H, fp32_routing=cfg["fp32_routing"], device=dev,
+                           dtype=torch.bfloat16)
         with torch.no_grad():
-            layer.w_router.normal_(0.0, 0.02, generator=torch.Generator(device=dev).manual_seed(1234))
             gen = torch.Generator(device=dev).manual_seed(1234 + rank)
             for w in (layer.w_gate, layer.w_up, layer.w_down):
                 w.normal_(0.0, 0.02, generator=gen)
-    x, grad_out = _make_inputs(dev, T, 99 + rank)
+    with torch.no_grad():
+        layer.w_router.normal_(0.0, router_std, generator=torch.Generator(device=dev).manual_seed(4321))
+    if cfg["zipf"]:
+        cg = torch.Generator().manual_seed(5)
+        order = torch.randperm(E, generator=cg)
+        expert_rank = torch.empty(E)
+        expert_rank[order] = torch.arange(1, E + 1, dtype=torch.float32)
+        layer.router_bias = (1.5 * torch.log(1.0 / expert_rank ** 1.2)).to(dev)
+    x, grad_out = _make_inputs(dev, T, d, 99 + rank)
     flops_step = layer_gemm_flops(T, K, d, H)
 
     def step(xin, gin):
@@ -242,16 +269,16 @@ def run_ours(args):
         "warmup": max(args.warmup, 3),
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if cfg["global_tokens"] else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) random-init weights)",
         "config": {
-            "workload": "cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16",
+            "workload": cfg["workload"],
             "model": "moe_layer_swiglu", "global_batch": T * world, "seq_len": 1,
             "parallelism": f"ep{world}" if world > 1 else "single",
             "tokens_per_rank": T,
-            "l2": "inputs larger than L2 (17.3 GB expert weights), no flush",
+            "l2": "inputs larger than L2 (expert weights 17.3 GB cfg4 / 22.5 GB cfg5), no flush",
             "gemm_flops_per_step": flops_step,
         },
         "roofline": {
@@ -274,7 +301,7 @@ def run_ours(args):
         "gpu_launches": launches,
         "clocks": clocks,
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "cfg4":
         line["cpu_baseline"] = cpu_baseline(steps=1, warmup=1)
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -429,6 +456,8 @@ def run_case(args):
 
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg4",
+                    help="layer workload: cfg4 (headline, default) or cfg5")
     ap.add_argument("--case", default="layer",
                     help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing")
     ap.add_argument("--experts", type=int, default=64, help="gmm-* cases: experts (cfg4 shapes)")

@@ -119,7 +119,8 @@ def all_to_all_rows(x, send_sizes, recv_sizes, group=None):
 def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.Tensor,
                    w_up_local: torch.Tensor, w_down_local: torch.Tensor, top_k: int,
                    num_experts: int, ops: EPOps | None = None, group=None,
-                   fp32_routing: bool = False) -> torch.Tensor:
+                   fp32_routing: bool = False,
+                   router_bias: torch.Tensor | None = None) -> torch.Tensor:
     """One expert-parallel SwiGLU MoE layer on this rank's tokens x [T, d].
 
     w_router [E, d] is replicated; w_*_local hold this rank's E/W experts
@@ -130,6 +131,8 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
     assert el * world == num_experts, "num_experts must equal world_size * local experts"
     T = x.shape[0]
     logits = x @ w_router.t()
+    if router_bias is not None:
+        logits = logits + router_bias
     if fp32_routing:
         logits = logits.float()
     weights, indices = ops.topk(logits, top_k)
@@ -165,7 +168,9 @@ class EPMoELayer(torch.nn.Module):
         self.w_gate = torch.nn.Parameter(torch.empty(el, hidden, d_model, **kw))
         self.w_up = torch.nn.Parameter(torch.empty(el, hidden, d_model, **kw))
         self.w_down = torch.nn.Parameter(torch.empty(el, d_model, hidden, **kw))
+        self.router_bias = None  # optional fixed per-expert logit bias [E]
 
     def forward(self, x):
         return ep_moe_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down, self.top_k,
-                              self.num_experts, group=self.group, fp32_routing=self.fp32_routing)
+                              self.num_experts, group=self.group, fp32_routing=self.fp32_routing,
+                              router_bias=self.router_bias)

@@ -26,10 +26,13 @@ from .unpermute_ops import unpermute
 
 def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Tensor,
                       w_up: torch.Tensor, w_down: torch.Tensor, top_k: int,
-                      fp32_routing: bool = False) -> torch.Tensor:
+                      fp32_routing: bool = False,
+                      router_bias: torch.Tensor | None = None) -> torch.Tensor:
     E = w_gate.shape[0]
     num_tokens = x.shape[0]
     logits = x @ w_router.t()
+    if router_bias is not None:
+        logits = logits + router_bias
     weights, indices = fused_topk_softmax(logits, top_k, fp32_routing=fp32_routing)
     permuted, row_id_map, offsets = permute(x, indices, E=E)
     gate = grouped_gemm(permuted, w_gate, offsets, trans_b=True)
@@ -53,6 +56,7 @@ class MoELayer(torch.nn.Module):
         self.w_gate = torch.nn.Parameter(torch.empty(num_experts, hidden, d_model, **kw))
         self.w_up = torch.nn.Parameter(torch.empty(num_experts, hidden, d_model, **kw))
         self.w_down = torch.nn.Parameter(torch.empty(num_experts, d_model, hidden, **kw))
+        self.router_bias = None  # optional fixed per-expert logit bias [E]
 
     @torch.no_grad()
     def init_normal(self, std: float = 0.02, generator=None) -> "MoELayer":
@@ -62,7 +66,7 @@ class MoELayer(torch.nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return moe_layer_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down,
-                                 self.top_k, self.fp32_routing)
+                                 self.top_k, self.fp32_routing, self.router_bias)
 
 
 def layer_gemm_flops(num_tokens: int, top_k: int, d_model: int, hidden: int,
