@@ -12,14 +12,14 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, overlapped):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
     try:
-        from moe_ops_b200.ep import ep_moe_forward
+        from moe_ops_b200.ep import ep_moe_forward, ep_moe_forward_overlapped
         from moe_ops_b200.moe_layer import moe_layer_forward
         from oracle.moe_oracle import rel_frobenius
 
@@ -35,7 +35,8 @@ def _worker(rank, world, port, q):
         sl = slice(rank * el, (rank + 1) * el)
         x = xs[rank].to(dev).requires_grad_(True)
         lg, lu, ld = (w[sl].to(dev).requires_grad_(True) for w in (wg, wu, wd))
-        out = ep_moe_forward(x, wr.to(dev), lg, lu, ld, K, E)
+        fwd = ep_moe_forward_overlapped if overlapped else ep_moe_forward
+        out = fwd(x, wr.to(dev), lg, lu, ld, K, E)
         out.backward(gos[rank].to(dev))
         # single-GPU layer (same kernels, all experts) over every rank's tokens
         fg, fu, fd = (w.to(dev).requires_grad_(True) for w in (wg, wu, wd))
@@ -57,13 +58,14 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_gpus_matches_single_gpu():
+@pytest.mark.parametrize("overlapped", [False, True])
+def test_ep_two_gpus_matches_single_gpu(overlapped):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, overlapped)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
