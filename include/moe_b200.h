@@ -48,6 +48,12 @@ const char* moe_last_error_string(void);
  * kernel gave up; 2 = an expert index outside [0, E) was seen by permute. */
 int moe_read_device_error(int* code_out);
 
+/* Failure-detection self-test (no counterpart in the reference): a kernel waits on an
+ * mbarrier nothing arrives at, with the bounded wait every GEMM pipeline wait uses.  After
+ * timeout_ns it gives up, writes 0 to *result (device int32), records device error 1 and
+ * returns; the context stays usable. */
+int moe_selftest_bounded_wait(uint64_t timeout_ns, int32_t* result, void* stream);
+
 /* ---------------------------------------------------------------- top-k softmax
  * Replaces tg::fused_topk_softmax_fwd
  * (triton_gmm_ops/fused_topk_softmax_ops.py:121-138, kernel :17-70).

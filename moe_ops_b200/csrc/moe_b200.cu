@@ -615,6 +615,26 @@ int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t
   return gmm_wgrad(A, grad_C, grad_B, offsets, plus_one, m_total, k, n, E, dtype, s);
 }
 
+// ---------------------------------------------------------------- bounded-wait self-test
+// One thread waits, with the same bounded wait the GEMM pipeline uses, on an mbarrier that
+// nothing arrives at.  The wait gives up after timeout_ns and records device error 1; the
+// kernel then returns normally, so the context stays usable.
+__global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int* result) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&bar), 1);
+    ptx::fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = ptx::wait_bounded(ptx::smem_u32(&bar), 0, &abort_flag, timeout_ns);
+    if (!ok) raise_device_error(1);
+    *result = ok ? 1 : 0;
+  }
+}
+
 // ---------------------------------------------------------------- permute without allocation
 // For callers that cannot allocate device memory at call time: code running inside a
 // captured stream or a custom allocator's own callbacks, runtimes that pre-plan every
@@ -657,6 +677,14 @@ int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, in
   return moe_permute(input, dtype, indices, num_tokens, topk, num_cols, E, num_out, permuted,
                      row_id_map, offsets, g_permute_scratch_ptr[dev],
                      kNoAllocScratchInts * sizeof(int32_t), stream);
+}
+
+int moe_selftest_bounded_wait(uint64_t timeout_ns, int32_t* result, void* stream) {
+  MOE_REQUIRE(result != nullptr, "selftest: result is NULL");
+  MOE_REQUIRE(timeout_ns <= 10000000000ull, "selftest: timeout above 10 s");
+  bounded_wait_selftest_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(timeout_ns, result);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
 }
 
 }  // extern "C"
