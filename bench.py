@@ -46,6 +46,9 @@ CONFIGS = {
 }
 CFG = CONFIGS["cfg4"]
 METRIC = "moe_layer_fwd_bwd_grouped_gemm_tflops"
+# Pure DRAM write bandwidth of this part, measured (torch zero_ on 5.8 GB, profiles/
+# hbm_write_bandwidth.md); the copy figure in MEASURED_PEAKS.json mixes reads and writes.
+HBM_WRITE_GBS = 3912.0
 
 
 def _dist_env():
@@ -221,8 +224,16 @@ def run_ours(args):
     ms_total = ev0.elapsed_time(ev1)
     launches = _lib.launch_count - launches0
     timing, _lib.gemm_timing = _lib.gemm_timing, None
-    gemm_ms = sum(a.elapsed_time(b) for _, a, b, _ in timing)
-    gemm_flops = sum(f for *_, f in timing)
+    gemm_ms = sum(t[1].elapsed_time(t[2]) for t in timing)
+    gemm_flops = sum(t[3] for t in timing)
+    # Per-launch roofline time: max(FLOPs / tensor peak, DRAM traffic / copy bandwidth,
+    # written bytes / pure-write bandwidth); writes are slower than reads on this part.
+    peaks_, _ = _peaks()
+    t_roof = 0.0
+    for t in timing:
+        flop_s = t[3] / (peaks_.get("bf16_tflops_sustained", 1400.0) * 1e12)
+        mem_s = max((t[4] + t[5]) / (peaks_["hbm_gbs"] * 1e9), t[5] / (HBM_WRITE_GBS * 1e9))
+        t_roof += max(flop_s, mem_s)
 
     # ------------------------------------------------------------ end to end (host buffers)
     x_host = x.cpu().pin_memory()
@@ -290,6 +301,10 @@ def run_ours(args):
             "frac": round(achieved / peak, 4) if achieved else None,
             "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
             "gemm_share_of_step": round(gemm_ms / ms_total, 4) if ms_total else None,
+            "gemm_time_vs_roofline": round(t_roof * 1e3 / gemm_ms, 4) if gemm_ms else None,
+            "roofline_note": "frac = achieved / tensor peak; gemm_time_vs_roofline = sum over "
+                             "launches of max(FLOP/tensor peak, DRAM bytes/copy BW, written "
+                             f"bytes/{HBM_WRITE_GBS:.0f} GB/s write BW) / measured GEMM time",
             "traffic": traffic.get("bytes_per_launch") if traffic else None,
         },
         "e2e": {

@@ -58,7 +58,11 @@ def _gmm_call(fn_name: str, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
             m_total, n, k, E, int(bool(trans_b)), _lib.dtype_code(x.dtype), _lib.stream_of(x))
         if timing is not None:
             ev1.record()
-            timing.append((fn_name, ev0, ev1, 2.0 * m_total * n * k))
+            es = x.element_size()
+            w_bytes, mk, mn = E * n * k * es, m_total * k * es, m_total * n * es
+            rd, wr = {"moe_gmm_fwd": (w_bytes + mk, mn), "moe_gmm_dgrad": (w_bytes + mn, mk),
+                      "moe_gmm_wgrad": (mk + mn, w_bytes)}[fn_name]
+            timing.append((fn_name, ev0, ev1, 2.0 * m_total * n * k, rd, wr))
     _lib.check(st, fn_name)
     _lib.count_launches(1)
 
