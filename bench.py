@@ -368,7 +368,7 @@ def run_reference(args):
     if rank != 0:
         return
     steps = max(1, min(args.steps, 3))
-    base = cpu_baseline(steps=steps, warmup=1)
+    base = cpu_baseline(steps=steps, warmup=1, sample_experts=args.cpu_sample_experts)
     ms_step = base["seconds_per_step"] * 1e3
     line = {
         "metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": world,
@@ -483,6 +483,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-experts", type=int, default=8,
+                    help="experts in the CPU baseline's sample (256 rows each)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -1,0 +1,22 @@
+"""bench.py's reference arm (the reference's PyTorch-native path on the CPU) prints one
+JSON line with the contract's keys; runs on the CPU."""
+import json
+import os
+import subprocess
+import sys
+
+from conftest import REPO
+
+
+def test_reference_arm_json_line():
+    out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "1", "--cpu-sample-experts", "1"], capture_output=True, text=True,
+                         timeout=600, cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "dtype", "config", "impl", "cpu_baseline", "e2e"):
+        assert key in line, key
+    assert line["impl"] == "reference"
+    assert line["value"] > 0 and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0
