@@ -10,7 +10,7 @@ from conftest import REPO
 
 def test_reference_arm_json_line():
     out = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference",
-                          "--steps", "1", "--warmup", "1", "--cpu-sample-experts", "1"], capture_output=True, text=True,
+                          "--steps", "1", "--warmup", "1", "--cpu-sample-experts", "2"], capture_output=True, text=True,
                          timeout=600, cwd=REPO)
     assert out.returncode == 0, out.stderr[-2000:]
     line = json.loads(out.stdout.strip().splitlines()[-1])
