@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <stdarg.h>
 #include <stdio.h>
@@ -29,13 +30,20 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+// Guards the per-device host-side caches (launch attributes, occupancy) that several host
+// threads may fill at once.
+static std::mutex g_cache_mu;
+
 int num_sms(int device) {
-  static int cache[64] = {0};
-  if (device >= 0 && device < 64 && cache[device] > 0) return cache[device];
+  static std::atomic<int> cache[64];
+  if (device >= 0 && device < 64) {
+    const int c = cache[device].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
     n = 148;
-  if (device >= 0 && device < 64) cache[device] = n;
+  if (device >= 0 && device < 64) cache[device].store(n, std::memory_order_relaxed);
   return n;
 }
 
@@ -101,10 +109,13 @@ static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   const int dev = current_device();
   static unsigned long long attr_set = 0;  // per-device bitmask, one per instantiation
   static int max_clusters[64] = {0};
-  if (dev < 64 && !(attr_set & (1ull << dev))) {
-    MOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)gmm::smem_bytes<CG>()));
-    attr_set |= 1ull << dev;
+  {
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    if (dev < 64 && !(attr_set & (1ull << dev))) {
+      MOE_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)gmm::smem_bytes<CG>()));
+      attr_set |= 1ull << dev;
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -122,6 +133,7 @@ static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   // is per GPC, so it can be below #SMs / 2).
   int grid = (num_sms(dev) / CG) * CG;
   if (CG == 2 && dev < 64) {
+    std::lock_guard<std::mutex> lock(g_cache_mu);
     if (max_clusters[dev] == 0) {
       cfg.gridDim = dim3(grid);
       int n = 0;
@@ -399,8 +411,17 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   MOE_LAUNCH_CHECK();
   const size_t rank_smem = (size_t)(kPermTileWarps + 2) * E * sizeof(int32_t);
   if (rank_smem > 48 * 1024) {
-    MOE_CUDA_CHECK(cudaFuncSetAttribute(permute_rank_kernel,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rank_smem));
+    // The opt-in limit only grows, so a concurrent call with a smaller E never lowers it
+    // under a launch that needs more.
+    static size_t rank_smem_set[64] = {0};
+    const int dev = current_device();
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    if (dev >= 64 || rank_smem > rank_smem_set[dev]) {
+      MOE_CUDA_CHECK(cudaFuncSetAttribute(permute_rank_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)rank_smem));
+      if (dev < 64) rank_smem_set[dev] = rank_smem;
+    }
   }
   permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
                                                           cnt, w.num_tiles, row_id_map, offsets);
