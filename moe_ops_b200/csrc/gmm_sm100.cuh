@@ -13,7 +13,8 @@
 //               contraction runs over the ragged rows of expert g.  X and Y are MN-major.
 //
 // and two CTA-group shapes:
-//   CG = 1  one CTA per tile, 128 x 256 tile, M=128 N=256 K=16 MMAs, 4 stages of 48 KB.
+//   CG = 1  one CTA per tile, 128 x 256 tile, M=128 N=256 K=16 MMAs, 4 stages of 48 KB
+//           (A in two 64-row boxes).
 //   CG = 2  a cluster of two CTAs (an SM pair) per 256 x 256 tile running cta_group::2
 //           MMAs (M=256, N=256): each CTA holds its own 128 rows of A and its own 128
 //           columns of B, so each SM streams 32 KB instead of 48 KB per 64-deep k-block;
@@ -24,7 +25,10 @@
 //           `tmem_full` barriers; both epilogues arrive on the leader's `tmem_empty` (the
 //           peer with a relaxed remote arrive).  No cluster-scope fence sits on the hot
 //           path: only a masked wgrad block hands its zeroed rows over with a
-//           release/acquire pair (`peer_done`).
+//           release/acquire pair (`peer_done`).  In kModeRows an expert's last tile of at
+//           most 128 rows is a half tile: M=128 pair MMAs with 64 rows per CTA.
+//           The host uses SM pairs for wgrad (P > 128) and single CTAs for kModeRows,
+//           where they measured faster.
 //
 // Warp roles (384 threads, one CTA per SM, persistent over a static tile stride):
 //   warp 0      TMA producer (one elected lane issues; it never waits on data).
@@ -178,6 +182,17 @@ __device__ __forceinline__ TileInfo decode_tile(const int* tile_prefix, const Pa
   return ti;
 }
 
+// A half tile is the last row tile of an expert in an SM pair when it holds at most 128
+// rows: the pair then runs cta_group::2 MMAs with M = 128, each CTA holding 64 rows of A
+// (and of the accumulator), so a short tail costs half a pair tile instead of a full one.
+// The accumulator of such a tile sits in TMEM as 64 rows x 256 columns per CTA folded into
+// 128 lanes x 128 columns: lanes 0-63 hold columns 0-127 and lanes 64-127 hold columns
+// 128-255 of rows 0-63.
+template <int MODE, int CG>
+__device__ __forceinline__ bool is_half_tile(const TileInfo& ti) {
+  return MODE == kModeRows && CG == 2 && ti.rows <= BMC;
+}
+
 // Packs 8 fp32 values into 8 16-bit values (round to nearest even) as one 16-byte vector.
 template <typename OutT>
 __device__ __forceinline__ uint4 pack8_16b(const uint32_t* v) {
@@ -308,12 +323,20 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           if (MODE == kModeRows) {
             // The leader expects the bytes of both CTAs; the peer's loads complete their
             // bytes on the leader's barrier (possibly before this expect, which is fine:
-            // the phase cannot complete before the leader's single arrival).
-            if (leader) ptx::mbar_arrive_expect_tx(full_local, CG * Sh::STAGE_BYTES);
+            // the phase cannot complete before the leader's single arrival).  A comes in
+            // 64-row boxes: two per CTA, or one for a half tile.
+            const bool half = is_half_tile<MODE, CG>(ti);
+            if (leader)
+              ptx::mbar_arrive_expect_tx(
+                  full_local, CG * (half ? Sh::STAGE_BYTES - Sh::A_BYTES / 2 : Sh::STAGE_BYTES));
             const int k0 = kb * BK;
             const int nb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
-            if (CG == 1) ptx::tma_load_2d(sa, &map_a, full_c, k0, ti.row0);
-            else ptx::tma_load_2d_pair(sa, &map_a, full_c, k0, ti.row0 + (int)rank * BMC);
+            const int a_rows = half ? BMC / 2 : BMC;
+            for (int j = 0; j < a_rows / 64; ++j) {
+              const int ar = ti.row0 + (int)rank * a_rows + j * 64;
+              if (CG == 1) ptx::tma_load_2d(sa + j * (64 * 128), &map_a, full_c, k0, ar);
+              else ptx::tma_load_2d_pair(sa + j * (64 * 128), &map_a, full_c, k0, ar);
+            }
             if (!B_MN) {
               if (CG == 1) ptx::tma_load_3d(sb, &map_b, full_c, k0, nb, ti.g);
               else ptx::tma_load_3d_pair(sb, &map_b, full_c, k0, nb, ti.g);
@@ -410,6 +433,8 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     // ---------------------------------------------------------- MMA issuer
     constexpr uint32_t idesc =
         ptx::make_idesc_f16(AB_FORMAT, A_MN ? 1 : 0, B_MN ? 1 : 0, Sh::TILE_M, BN);
+    constexpr uint32_t idesc_half =
+        ptx::make_idesc_f16(AB_FORMAT, A_MN ? 1 : 0, B_MN ? 1 : 0, BMC, BN);
     // K-major: rows of 128 bytes, 8-row atoms 1024 bytes apart; a K=16 step is +32 bytes.
     // MN-major: 64-element column chunks BK*128 bytes apart (LBO), 8-k-row atoms 1024
     // bytes apart (SBO); a K=16 step is two atoms (+2048 bytes).
@@ -424,6 +449,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       if (!wait_local(ptx::smem_u32(&s.tmem_empty[buf]), acc_phase ^ 1, abort_flag)) break;
       ptx::tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * BN;
+      const uint32_t tile_idesc = is_half_tile<MODE, CG>(ti) ? idesc_half : idesc;
       bool ok = true;
       for (int kb = 0; kb < ti.nkb; ++kb) {
         if (!wait_local(ptx::smem_u32(&s.full[stage]), phase, abort_flag)) {
@@ -440,7 +466,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                                      : ptx::make_sw128_desc(sa + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? ptx::make_sw128_desc(sb + kk * 2048, kLboMN, 1024)
                                      : ptx::make_sw128_desc(sb + kk * 32, 16, 1024);
-            ptx::mma_f16_ss<CG>(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+            ptx::mma_f16_ss<CG>(d_tmem, ad, bd, tile_idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           const uint32_t eb = ptx::smem_u32(&s.empty[stage]);
           ptx::mma_commit<CG>(eb);
@@ -487,29 +513,39 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       if (!wait_local(ptx::smem_u32(&s.tmem_full[buf]), acc_phase, abort_flag)) break;
       ptx::tc_fence_after();
       const int n0 = ti.n_blk * BN;
-      const int col_lo = h * (BN / 2);
+      // Full tile: this warp reads TMEM lanes of rows 32q..32q+31 and tile columns
+      // [128h, 128h+128).  Half tile: lanes 32q.. hold rows 32(q&1).. of the CTA's 64 and
+      // tile columns from 128(q>>1); the warp reads 64 of those columns from TMEM column 64h.
+      const bool half = is_half_tile<MODE, CG>(ti);
+      const int rq = half ? (q & 1) : q;                 // 32-row group of this warp
+      const int tcol = half ? h * 64 : h * (BN / 2);    // first TMEM column read
+      const int col_lo = half ? (q >> 1) * (BN / 2) + h * 64 : h * (BN / 2);
+      const int ncols = half ? 64 : BN / 2;
       const int valid_cols = min(BN, p.n_out - n0);
       int valid_rows, row_base;
-      OutT* tile_ptr;  // element (0, 0) of this CTA's 128 rows of the tile
+      OutT* tile_ptr;  // element (0, 0) of this CTA's rows of the tile
       if (MODE == kModeRows) {
-        valid_rows = min(BMC, ti.rows - (int)rank * BMC);
-        row_base = ti.row0 + (int)rank * BMC;
+        const int cta_rows = half ? BMC / 2 : BMC;
+        valid_rows = min(cta_rows, ti.rows - (int)rank * cta_rows);
+        row_base = ti.row0 + (int)rank * cta_rows;
         tile_ptr = out + (int64_t)row_base * p.n_out + n0;
       } else {
         row_base = ti.m_blk * Sh::TILE_M + (int)rank * BMC;  // row inside expert g
         valid_rows = min(BMC, p.p_out - row_base);
         tile_ptr = out + ((int64_t)ti.g * p.p_out + row_base) * p.n_out + n0;
       }
-      // TMA stores clip at the output's edges, so they serve every wgrad tile and the
-      // row tiles whose 128 rows all belong to the expert; the others store with masks so
-      // they never touch the next expert's rows.
-      const bool use_tma = MODE == kModeWgrad || valid_rows == BMC;
+      // TMA stores clip at the output's edges, so they serve every wgrad tile and every
+      // warp whose 32 rows all belong to the expert; the others store with masks so they
+      // never touch the next expert's rows.  A warp with no valid row stores nothing.
+      const bool use_tma = MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows;
 #if MOE_GMM_EPI_EXPERIMENT == 2
       const int nchunks = 0;
 #else
-      const int nchunks = max(0, min(BN / 2, valid_cols - col_lo) + 31) / 32;
+      const int nchunks = (MODE == kModeRows && valid_rows <= rq * 32)
+                              ? 0
+                              : max(0, min(ncols, valid_cols - col_lo) + 31) / 32;
 #endif
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + col_lo;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + tcol;
       uint32_t v[32];
       const bool has_acc = ti.nkb > 0;
       if (has_acc && nchunks > 0) {
@@ -543,8 +579,8 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           __syncwarp();
           if (lane == 0) {
             const int cx = n0 + col_lo + c * 32;
-            if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + q * 32);
-            else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + q * 32, ti.g);
+            if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
+            else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
             ptx::bulk_commit_group();
           }
           if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
@@ -557,7 +593,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           const int rr = rd_row0 + i * 8;
           const int phys = rd_chunk ^ ((rr >> 1) & 3);
           const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
-          const int row = q * 32 + rr;
+          const int row = rq * 32 + rr;
 #if MOE_GMM_EPI_EXPERIMENT == 0
           if (row < valid_rows && col < valid_cols)
             *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;

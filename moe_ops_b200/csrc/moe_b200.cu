@@ -203,14 +203,15 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     MOE_LAUNCH_CHECK();
     return MOE_OK;
   }
-  // SM pairs (256-row tiles) pay off when experts have many rows; with few rows per
-  // expert the 128-row tiles waste less of the last, partial tile.
-  const int cg = pick_cg(m_total >= 384ll * E ? 2 : 1);
+  // Single-CTA tiles: measured on B200 against SM pairs (with half tail tiles) for 256 to
+  // 2048 rows per expert at d=4096 / H=11008 shapes, they run 3-15 % faster in this mode.
+  const int cg = pick_cg(1);
   const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
     const uint64_t dims[2] = {(uint64_t)k_red, (uint64_t)m_total};
-    const uint32_t box[2] = {(uint32_t)gmm::BK, (uint32_t)gmm::BMC};
+    // 64-row boxes: two per CTA, one per CTA of a half tile.
+    const uint32_t box[2] = {(uint32_t)gmm::BK, 64u};
     int rc = make_map(&ma, A, dtype, 2, dims, box);
     if (rc) return rc;
   }

@@ -90,6 +90,14 @@ def test_partial_tiles(cuda_dev, cta_group, dtype):
     _run([100, 250, 130, 300], K=136, N=200, dtype=dtype, trans_b=False, seed=3)
 
 
+@pytest.mark.parametrize("trans_b", [True, False])
+def test_tail_tile_boundaries(cuda_dev, cta_group, trans_b):
+    # Last row tiles of 32, 64, 65, 96, 128 and 127 rows (half pair tiles with 0, 1 or 2
+    # full 32-row groups per CTA), 192 and 255 (full pair tiles with a short peer).
+    _run([32, 64, 65, 96, 192, 255, 320, 383, 128 + 256], K=128, N=320, dtype=torch.bfloat16,
+         trans_b=trans_b, seed=10)
+
+
 def test_unaligned_falls_back_to_cuda_cores(cuda_dev):
     # K=130 rows are not 16-byte multiples: served by the CUDA-core kernel, same contract.
     _run([100, 250, 130, 300], K=130, N=202, dtype=torch.bfloat16, seed=4)
