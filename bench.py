@@ -242,10 +242,23 @@ def run_ours(args):
     x_dev = torch.empty_like(x)
     g_dev = torch.empty_like(grad_out)
 
+    copy_stream = torch.cuda.Stream(device=dev)
+
     def e2e_step():
+        # The activations are copied on the compute stream (the forward needs them first);
+        # the output gradient is copied on a copy stream while the forward runs, and the
+        # backward waits for it.  Both copies happen every step.
+        main = torch.cuda.current_stream(dev)
         x_dev.copy_(x_host, non_blocking=True)
-        g_dev.copy_(g_host, non_blocking=True)
-        out = step(x_dev, g_dev)
+        copy_stream.wait_stream(main)  # the previous step's backward has read g_dev
+        with torch.cuda.stream(copy_stream):
+            g_dev.copy_(g_host, non_blocking=True)
+        for p in layer.parameters():
+            p.grad = None
+        xin = x_dev.detach().requires_grad_(True)
+        out = layer(xin)
+        main.wait_stream(copy_stream)
+        out.backward(g_dev)
         res_host.copy_(out.detach().float().sum().reshape(1), non_blocking=True)
 
     e2e_step()
@@ -312,6 +325,8 @@ def run_ours(args):
             "ms_per_step": round(e2e_ms / args.steps, 4),
             "h2d_bytes_per_step": x.numel() * 2 + grad_out.numel() * 2,
             "d2h_bytes_per_step": 4,
+            "note": "pinned host inputs copied every step: activations before the forward, "
+                    "the output gradient on a copy stream during the forward",
         },
         "gpu_launches": launches,
         "clocks": clocks,
