@@ -160,6 +160,18 @@ int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t
                   int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
                   int32_t num_experts, int trans_b, int dtype, void* stream);
 
+/* Gate and up projections of a SwiGLU expert layer with the SwiGLU applied, in one launch:
+ *   gate = A @ B_gate[e]^T, up = A @ B_up[e]^T (trans_b; else A @ B[e]),
+ *   h = rnd(rnd(silu(gate)) * up)
+ * over the rows of each expert; B_gate / B_up as B of moe_gmm_fwd, gate / up / h
+ * [M_total, N].  The three outputs equal two moe_gmm_fwd calls followed by moe_swiglu_fwd
+ * bit for bit; gate and up are kept for the backward.  Replaces the reference layer's
+ * two grouped_gemm calls and `F.silu(gate) * up` (tests/test_moe.py:80-82). */
+int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, void* gate,
+                        void* up, void* h, const int32_t* offsets, int32_t num_offsets,
+                        int64_t m_total, int64_t n, int64_t k, int32_t num_experts, int trans_b,
+                        int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

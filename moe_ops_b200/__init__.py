@@ -23,6 +23,7 @@ from .grouped_gemm_ops import grouped_gemm, supports_tma
 from .permute_ops import permute, permute_backward
 from .unpermute_ops import unpermute, unpermute_forward, unpermute_backward
 from .fused_topk_softmax_ops import fused_topk_softmax
+from .gate_up_ops import grouped_gemm_swiglu
 
 __all__ = [
     "grouped_gemm",
@@ -33,4 +34,6 @@ __all__ = [
     "unpermute_forward",
     "unpermute_backward",
     "fused_topk_softmax",
+    # beyond the reference's API: gate/up projections with the SwiGLU in one launch
+    "grouped_gemm_swiglu",
 ]

@@ -47,6 +47,8 @@ SIGNATURES = {
                                    _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "moe_gmm_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
                              _c_int, _c_int, _c_ptr]),
+    "moe_gmm_gate_up_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32,
+                                     _c_i64, _c_i64, _c_i64, _c_i32, _c_int, _c_int, _c_ptr]),
     "moe_gmm_dgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
                                _c_int, _c_int, _c_ptr]),
     "moe_gmm_wgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,

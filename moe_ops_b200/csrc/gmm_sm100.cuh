@@ -60,6 +60,7 @@
 
 #include "common.cuh"
 #include "sm100_ptx.cuh"
+#include "swiglu.cuh"
 
 #include <type_traits>
 
@@ -91,7 +92,12 @@ struct Shape {
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA per stage
 };
 
-enum Mode { kModeRows = 0, kModeWgrad = 1 };
+enum Mode { kModeRows = 0, kModeWgrad = 1, kModeGateUp = 2 };
+
+// Output columns one tile covers: a gate/up tile holds 128 gate and 128 up columns in its
+// 256-column accumulator and writes 128 columns of each output.
+template <int MODE>
+__host__ __device__ constexpr int tile_out_cols() { return MODE == kModeGateUp ? BN / 2 : BN; }
 
 template <int CG>
 struct SmemLayout {
@@ -120,7 +126,10 @@ struct Params {
   int n_out;             // output columns (kModeRows: Nout, kModeWgrad: Q)
   int p_out;             // kModeWgrad: output rows per expert (P)
   int k_red;             // kModeRows: contraction length (Kc)
-  void* out;             // kModeRows: C [m_total, n_out]; kModeWgrad: [E, p_out, n_out]
+  void* out;             // kModeRows: C [m_total, n_out]; kModeWgrad: [E, p_out, n_out];
+                         // kModeGateUp: h = silu(gate) * up [m_total, n_out]
+  void* out_gate;        // kModeGateUp: gate = A . B_gate^T [m_total, n_out]
+  void* out_up;          // kModeGateUp: up = A . B_up^T [m_total, n_out]
 };
 
 struct TileInfo {
@@ -144,8 +153,8 @@ __device__ __forceinline__ void group_range(const Params& p, int g, int& start, 
 template <int MODE, int CG>
 __device__ __forceinline__ int tiles_of_group(const Params& p, int rows) {
   constexpr int TM = Shape<CG>::TILE_M;
-  const int nt = (p.n_out + BN - 1) / BN;
-  if (MODE == kModeRows) return ((rows + TM - 1) / TM) * nt;
+  const int nt = (p.n_out + tile_out_cols<MODE>() - 1) / tile_out_cols<MODE>();
+  if (MODE != kModeWgrad) return ((rows + TM - 1) / TM) * nt;
   return ((p.p_out + TM - 1) / TM) * nt;
 }
 
@@ -164,7 +173,7 @@ __device__ __forceinline__ TileInfo decode_tile(const int* tile_prefix, const Pa
   const int local = t - tile_prefix[lo];
   int start, rows;
   group_range(p, lo, start, rows);
-  if (MODE == kModeRows) {
+  if (MODE != kModeWgrad) {
     const int mt = (rows + TM - 1) / TM;
     ti.m_blk = local % mt;
     ti.n_blk = local / mt;
@@ -224,7 +233,10 @@ __device__ __forceinline__ bool wait_local(uint32_t bar, uint32_t parity, volati
 template <int MODE, int CG, int AB_FORMAT, bool A_MN, bool B_MN, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
 gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const __grid_constant__ CUtensorMap map_c, const Params p) {
+                 const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_b2,
+                 const __grid_constant__ CUtensorMap map_c2, const __grid_constant__ CUtensorMap map_c3,
+                 const Params p) {
+  static_assert(MODE != kModeGateUp || CG == 1, "gate/up tiles run on single CTAs");
   using Sh = Shape<CG>;
   constexpr int STAGES = Sh::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -256,6 +268,11 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     ptx::prefetch_tensormap(&map_a);
     ptx::prefetch_tensormap(&map_b);
     ptx::prefetch_tensormap(&map_c);
+    if (MODE == kModeGateUp) {
+      ptx::prefetch_tensormap(&map_b2);
+      ptx::prefetch_tensormap(&map_c2);
+      ptx::prefetch_tensormap(&map_c3);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc<CG>(ptx::smem_u32(&s.tmem_base), kTmemCols);
@@ -320,7 +337,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           // The leader's full barrier, addressed for the cluster.
           const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
           const uint32_t full_c = CG == 1 ? full_local : ptx::mapa_shared(full_local, 0);
-          if (MODE == kModeRows) {
+          if (MODE != kModeWgrad) {
             // The leader expects the bytes of both CTAs; the peer's loads complete their
             // bytes on the leader's barrier (possibly before this expect, which is fine:
             // the phase cannot complete before the leader's single arrival).  A comes in
@@ -330,14 +347,26 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               ptx::mbar_arrive_expect_tx(
                   full_local, CG * (half ? Sh::STAGE_BYTES - Sh::A_BYTES / 2 : Sh::STAGE_BYTES));
             const int k0 = kb * BK;
-            const int nb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+            const int nb = ti.n_blk * tile_out_cols<MODE>() + (int)rank * Sh::B_COLS;
             const int a_rows = half ? BMC / 2 : BMC;
             for (int j = 0; j < a_rows / 64; ++j) {
               const int ar = ti.row0 + (int)rank * a_rows + j * 64;
               if (CG == 1) ptx::tma_load_2d(sa + j * (64 * 128), &map_a, full_c, k0, ar);
               else ptx::tma_load_2d_pair(sa + j * (64 * 128), &map_a, full_c, k0, ar);
             }
-            if (!B_MN) {
+            if (MODE == kModeGateUp) {
+              // B rows 0-127: gate columns nb.., rows 128-255: the same up columns.
+              if (!B_MN) {
+                ptx::tma_load_3d(sb, &map_b, full_c, k0, nb, ti.g);
+                ptx::tma_load_3d(sb + (BN / 2) * 128, &map_b2, full_c, k0, nb, ti.g);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                  ptx::tma_load_3d(sb + j * (BK * 128), &map_b, full_c, nb + j * 64, k0, ti.g);
+                  ptx::tma_load_3d(sb + (2 + j) * (BK * 128), &map_b2, full_c, nb + j * 64, k0, ti.g);
+                }
+              }
+            } else if (!B_MN) {
               if (CG == 1) ptx::tma_load_3d(sb, &map_b, full_c, k0, nb, ti.g);
               else ptx::tma_load_3d_pair(sb, &map_b, full_c, k0, nb, ti.g);
             } else {
@@ -512,97 +541,178 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const uint32_t acc_phase = (acc >> 1) & 1;
       if (!wait_local(ptx::smem_u32(&s.tmem_full[buf]), acc_phase, abort_flag)) break;
       ptx::tc_fence_after();
-      const int n0 = ti.n_blk * BN;
-      // Full tile: this warp reads TMEM lanes of rows 32q..32q+31 and tile columns
-      // [128h, 128h+128).  Half tile: lanes 32q.. hold rows 32(q&1).. of the CTA's 64 and
-      // tile columns from 128(q>>1); the warp reads 64 of those columns from TMEM column 64h.
-      const bool half = is_half_tile<MODE, CG>(ti);
-      const int rq = half ? (q & 1) : q;                 // 32-row group of this warp
-      const int tcol = half ? h * 64 : h * (BN / 2);    // first TMEM column read
-      const int col_lo = half ? (q >> 1) * (BN / 2) + h * 64 : h * (BN / 2);
-      const int ncols = half ? 64 : BN / 2;
-      const int valid_cols = min(BN, p.n_out - n0);
-      int valid_rows, row_base;
-      OutT* tile_ptr;  // element (0, 0) of this CTA's rows of the tile
-      if (MODE == kModeRows) {
-        const int cta_rows = half ? BMC / 2 : BMC;
-        valid_rows = min(cta_rows, ti.rows - (int)rank * cta_rows);
-        row_base = ti.row0 + (int)rank * cta_rows;
-        tile_ptr = out + (int64_t)row_base * p.n_out + n0;
-      } else {
-        row_base = ti.m_blk * Sh::TILE_M + (int)rank * BMC;  // row inside expert g
-        valid_rows = min(BMC, p.p_out - row_base);
-        tile_ptr = out + ((int64_t)ti.g * p.p_out + row_base) * p.n_out + n0;
-      }
-      // TMA stores clip at the output's edges, so they serve every wgrad tile and every
-      // warp whose 32 rows all belong to the expert; the others store with masks so they
-      // never touch the next expert's rows.  A warp with no valid row stores nothing.
-      const bool use_tma = MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows;
-#if MOE_GMM_EPI_EXPERIMENT == 2
-      const int nchunks = 0;
-#else
-      const int nchunks = (MODE == kModeRows && valid_rows <= rq * 32)
-                              ? 0
-                              : max(0, min(ncols, valid_cols - col_lo) + 31) / 32;
-#endif
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + tcol;
-      uint32_t v[32];
-      const bool has_acc = ti.nkb > 0;
-      if (has_acc && nchunks > 0) {
-        ptx::tmem_ld_32x32b_x32(tbase, v);
-        ptx::tmem_wait_ld();
-      }
-      for (int c = 0; c < nchunks; ++c) {
-        uint32_t w[16];
-        if (has_acc) {
+      if constexpr (MODE == kModeGateUp) {
+        // Warp (q, h) owns rows 32q..32q+31 and output columns [64h, 64h+64) of the tile:
+        // two 32-column chunks, each read from the gate half (TMEM column c) and the up half
+        // (column 128 + c) of the accumulator.  gate and up are rounded to 16 bits as the
+        // plain GEMM stores them, then h = rnd(rnd(silu(gate)) * up) as the SwiGLU kernel
+        // computes it, so the three outputs equal GEMM + GEMM + SwiGLU bit for bit.
+        const int n0 = ti.n_blk * (BN / 2);
+        const int valid_cols = min(BN / 2, p.n_out - n0);
+        const int valid_rows = min(BMC, ti.rows);
+        const int row_base = ti.row0;
+        const bool use_tma = (q + 1) * 32 <= valid_rows;
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+        // Stages one 32 x 32 block of 16-bit words (row per lane) and stores it to `dst`.
+        auto put = [&](const uint32_t* wd, const CUtensorMap* map, OutT* dst, int col) {
+          if (lane == 0) ptx::bulk_wait_group_read<0>();
+          __syncwarp();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const uint4 u = pack8_16b<OutT>(&v[i * 8]);
-            w[i * 4 + 0] = u.x; w[i * 4 + 1] = u.y; w[i * 4 + 2] = u.z; w[i * 4 + 3] = u.w;
+            const int phys = i ^ ((wr_row >> 1) & 3);
+            *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
+                make_uint4(wd[i * 4 + 0], wd[i * 4 + 1], wd[i * 4 + 2], wd[i * 4 + 3]);
           }
-          if (c + 1 < nchunks) ptx::tmem_ld_32x32b_x32(tbase + (c + 1) * 32, v);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = 0u;
-        }
-        // The previous TMA store from this buffer must have finished reading it.
-        if (lane == 0) ptx::bulk_wait_group_read<0>();
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int phys = i ^ ((wr_row >> 1) & 3);
-          *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
-              make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
-        }
-        if (use_tma) {
-          ptx::fence_proxy_async_smem();
+          if (use_tma) {
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              ptx::tma_store_2d(map, cbuf_u32, n0 + col, row_base + q * 32);
+              ptx::bulk_commit_group();
+            }
+            return;
+          }
           __syncwarp();
-          if (lane == 0) {
-            const int cx = n0 + col_lo + c * 32;
-            if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
-            else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
-            ptx::bulk_commit_group();
-          }
-          if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
-          continue;
-        }
-        __syncwarp();
-        const int col = col_lo + c * 32 + rd_chunk * 8;  // first column of this lane's chunk
+          const int cc = col + rd_chunk * 8;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int rr = rd_row0 + i * 8;
-          const int phys = rd_chunk ^ ((rr >> 1) & 3);
-          const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
-          const int row = rq * 32 + rr;
-#if MOE_GMM_EPI_EXPERIMENT == 0
-          if (row < valid_rows && col < valid_cols)
-            *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;
-#else
-          if (u.x == 0x7fc00001u && row < 0 && col < 0) *reinterpret_cast<uint4*>(tile_ptr) = u;
-#endif
+          for (int i = 0; i < 4; ++i) {
+            const int rr = rd_row0 + i * 8;
+            const int phys = rd_chunk ^ ((rr >> 1) & 3);
+            const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
+            const int row = q * 32 + rr;
+            if (row < valid_rows && cc < valid_cols)
+              *reinterpret_cast<uint4*>(dst + (int64_t)(row_base + row) * p.n_out + n0 + cc) = u;
+          }
+          __syncwarp();
+        };
+        if (valid_rows > q * 32) {
+          for (int c = 0; c < 2; ++c) {
+            const int col = h * 64 + c * 32;
+            if (col >= valid_cols) break;
+            uint32_t vg[32], vu[32];
+            ptx::tmem_ld_32x32b_x32(tbase + col, vg);
+            ptx::tmem_ld_32x32b_x32(tbase + BN / 2 + col, vu);
+            ptx::tmem_wait_ld();
+            uint32_t wd[16];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 x = pack8_16b<OutT>(&vg[i * 8]);
+              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
+            }
+            put(wd, &map_c2, static_cast<OutT*>(p.out_gate), col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 x = pack8_16b<OutT>(&vu[i * 8]);
+              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
+            }
+            put(wd, &map_c3, static_cast<OutT*>(p.out_up), col);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float gq = rnd<OutT>(__uint_as_float(vg[i]));
+              const float uq = rnd<OutT>(__uint_as_float(vu[i]));
+              vg[i] = __float_as_uint(rnd<OutT>(gq * sigmoid_f32(gq)) * uq);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 x = pack8_16b<OutT>(&vg[i * 8]);
+              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
+            }
+            put(wd, &map_c, out, col);
+          }
         }
-        __syncwarp();
-        if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
+      } else {
+        const int n0 = ti.n_blk * BN;
+        // Full tile: this warp reads TMEM lanes of rows 32q..32q+31 and tile columns
+        // [128h, 128h+128).  Half tile: lanes 32q.. hold rows 32(q&1).. of the CTA's 64 and
+        // tile columns from 128(q>>1); the warp reads 64 of those columns from TMEM column 64h.
+        const bool half = is_half_tile<MODE, CG>(ti);
+        const int rq = half ? (q & 1) : q;                 // 32-row group of this warp
+        const int tcol = half ? h * 64 : h * (BN / 2);    // first TMEM column read
+        const int col_lo = half ? (q >> 1) * (BN / 2) + h * 64 : h * (BN / 2);
+        const int ncols = half ? 64 : BN / 2;
+        const int valid_cols = min(BN, p.n_out - n0);
+        int valid_rows, row_base;
+        OutT* tile_ptr;  // element (0, 0) of this CTA's rows of the tile
+        if (MODE == kModeRows) {
+          const int cta_rows = half ? BMC / 2 : BMC;
+          valid_rows = min(cta_rows, ti.rows - (int)rank * cta_rows);
+          row_base = ti.row0 + (int)rank * cta_rows;
+          tile_ptr = out + (int64_t)row_base * p.n_out + n0;
+        } else {
+          row_base = ti.m_blk * Sh::TILE_M + (int)rank * BMC;  // row inside expert g
+          valid_rows = min(BMC, p.p_out - row_base);
+          tile_ptr = out + ((int64_t)ti.g * p.p_out + row_base) * p.n_out + n0;
+        }
+        // TMA stores clip at the output's edges, so they serve every wgrad tile and every
+        // warp whose 32 rows all belong to the expert; the others store with masks so they
+        // never touch the next expert's rows.  A warp with no valid row stores nothing.
+        const bool use_tma = MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows;
+  #if MOE_GMM_EPI_EXPERIMENT == 2
+        const int nchunks = 0;
+  #else
+        const int nchunks = (MODE == kModeRows && valid_rows <= rq * 32)
+                                ? 0
+                                : max(0, min(ncols, valid_cols - col_lo) + 31) / 32;
+  #endif
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + tcol;
+        uint32_t v[32];
+        const bool has_acc = ti.nkb > 0;
+        if (has_acc && nchunks > 0) {
+          ptx::tmem_ld_32x32b_x32(tbase, v);
+          ptx::tmem_wait_ld();
+        }
+        for (int c = 0; c < nchunks; ++c) {
+          uint32_t w[16];
+          if (has_acc) {
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint4 u = pack8_16b<OutT>(&v[i * 8]);
+              w[i * 4 + 0] = u.x; w[i * 4 + 1] = u.y; w[i * 4 + 2] = u.z; w[i * 4 + 3] = u.w;
+            }
+            if (c + 1 < nchunks) ptx::tmem_ld_32x32b_x32(tbase + (c + 1) * 32, v);
+          } else {
+  #pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = 0u;
+          }
+          // The previous TMA store from this buffer must have finished reading it.
+          if (lane == 0) ptx::bulk_wait_group_read<0>();
+          __syncwarp();
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int phys = i ^ ((wr_row >> 1) & 3);
+            *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
+                make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
+          }
+          if (use_tma) {
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int cx = n0 + col_lo + c * 32;
+              if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
+              else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
+              ptx::bulk_commit_group();
+            }
+            if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
+            continue;
+          }
+          __syncwarp();
+          const int col = col_lo + c * 32 + rd_chunk * 8;  // first column of this lane's chunk
+  #pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = rd_row0 + i * 8;
+            const int phys = rd_chunk ^ ((rr >> 1) & 3);
+            const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
+            const int row = rq * 32 + rr;
+  #if MOE_GMM_EPI_EXPERIMENT == 0
+            if (row < valid_rows && col < valid_cols)
+              *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;
+  #else
+            if (u.x == 0x7fc00001u && row < 0 && col < 0) *reinterpret_cast<uint4*>(tile_ptr) = u;
+  #endif
+          }
+          __syncwarp();
+          if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
+        }
       }
       ptx::tc_fence_before();
       __syncwarp();

@@ -103,8 +103,10 @@ static int make_map(CUtensorMap* map, const void* base, int dtype, int rank, con
 
 // ---------------------------------------------------------------- GEMM launchers
 template <int MODE, int CG, int FMT, bool A_MN, bool B_MN, typename OutT>
+// `extra` (kModeGateUp): the up-projection weights' map, then the gate and up output maps.
 static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                        const gmm::Params& p, cudaStream_t stream) {
+                        const gmm::Params& p, cudaStream_t stream,
+                        const CUtensorMap* extra = nullptr) {
   auto kern = gmm::gmm_sm100_kernel<MODE, CG, FMT, A_MN, B_MN, OutT>;
   const int dev = current_device();
   static unsigned long long attr_set = 0;  // per-device bitmask, one per instantiation
@@ -146,7 +148,8 @@ static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   if (getenv("MOE_B200_DEBUG"))
     fprintf(stderr, "[moe_b200] gmm launch: mode=%d cg=%d grid=%d smem=%zu\n", MODE, CG, grid,
             gmm::smem_bytes<CG>());
-  MOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p));
+  MOE_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, extra ? extra[0] : mb,
+                                    extra ? extra[1] : mc, extra ? extra[2] : mc, p));
   MOE_LAUNCH_CHECK();
   return MOE_OK;
 }
@@ -233,7 +236,7 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     int rc = make_map(&mc, C, dtype, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   }
-  gmm::Params p;
+  gmm::Params p = {};
   p.offsets = offsets;
   p.offsets_plus_one = plus_one;
   p.num_groups = E;
@@ -295,7 +298,7 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
     int rc = make_map(&mo, Out, dtype, 3, dims, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
   }
-  gmm::Params p;
+  gmm::Params p = {};
   p.offsets = offsets;
   p.offsets_plus_one = plus_one;
   p.num_groups = E;
@@ -635,6 +638,77 @@ int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t
   // trans_b: grad_B[e] [N, K] = grad_C_e^T A_e;  else grad_B[e] [K, N] = A_e^T grad_C_e.
   if (trans_b) return gmm_wgrad(grad_C, A, grad_B, offsets, plus_one, m_total, n, k, E, dtype, s);
   return gmm_wgrad(A, grad_C, grad_B, offsets, plus_one, m_total, k, n, E, dtype, s);
+}
+
+int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, void* gate,
+                        void* up, void* h, const int32_t* offsets, int32_t num_offsets,
+                        int64_t m_total, int64_t n, int64_t k, int32_t E, int trans_b, int dtype,
+                        void* stream) {
+  int rc = check_gmm_args(A, B_gate, gate, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  MOE_REQUIRE((B_up && up && h) || m_total == 0 || E == 0, "gmm_gate_up: NULL operand");
+  if (E == 0 || m_total == 0 || n == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const int plus_one = num_offsets == E + 1;
+  const bool tc = dtype != MOE_F32 && k % 8 == 0 && n % 8 == 0 && k > 0 && E <= gmm::kMaxGroups &&
+                  aligned16(A) && aligned16(B_gate) && aligned16(B_up) && aligned16(gate) &&
+                  aligned16(up) && aligned16(h) && m_total < (1ll << 31) && n < (1ll << 31) &&
+                  k < (1ll << 31);
+  if (!tc) {
+    // Same results from the separate kernels: two grouped GEMMs, then the SwiGLU pass.
+    rc = gmm_rows(A, B_gate, gate, offsets, plus_one, m_total, n, k, E, !trans_b, dtype, s);
+    if (rc) return rc;
+    rc = gmm_rows(A, B_up, up, offsets, plus_one, m_total, n, k, E, !trans_b, dtype, s);
+    if (rc) return rc;
+    return moe_swiglu_fwd(gate, up, h, m_total * n, dtype, stream);
+  }
+  CUtensorMap maps[6];  // A, B_gate, h, B_up, gate, up
+  {
+    const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m_total};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, 64u};
+    if ((rc = make_map(&maps[0], A, dtype, 2, dims, box))) return rc;
+  }
+  for (int i = 0; i < 2; ++i) {
+    const void* B = i == 0 ? B_gate : B_up;
+    CUtensorMap* m = i == 0 ? &maps[1] : &maps[3];
+    if (trans_b) {  // [E, n, k]: K-major, 128 weight rows per box
+      const uint64_t dims[3] = {(uint64_t)k, (uint64_t)n, (uint64_t)E};
+      const uint32_t box[3] = {(uint32_t)gmm::BK, (uint32_t)(gmm::BN / 2), 1};
+      if ((rc = make_map(m, B, dtype, 3, dims, box))) return rc;
+    } else {  // [E, k, n]: MN-major, 64-column boxes
+      const uint64_t dims[3] = {(uint64_t)n, (uint64_t)k, (uint64_t)E};
+      const uint32_t box[3] = {64, (uint32_t)gmm::BK, 1};
+      if ((rc = make_map(m, B, dtype, 3, dims, box))) return rc;
+    }
+  }
+  void* outs[3] = {h, gate, up};
+  const int out_slot[3] = {2, 4, 5};
+  for (int i = 0; i < 3; ++i) {
+    const uint64_t dims[2] = {(uint64_t)n, (uint64_t)m_total};
+    const uint32_t box[2] = {32, 32};
+    if ((rc = make_map(&maps[out_slot[i]], outs[i], dtype, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+  }
+  gmm::Params p = {};
+  p.offsets = offsets;
+  p.offsets_plus_one = plus_one;
+  p.num_groups = E;
+  p.m_total = m_total;
+  p.n_out = (int)n;
+  p.k_red = (int)k;
+  p.out = h;
+  p.out_gate = gate;
+  p.out_up = up;
+  const CUtensorMap* extra = &maps[3];
+  if (dtype == MOE_BF16)
+    return trans_b ? launch_sm100<gmm::kModeGateUp, 1, 1, false, false, __nv_bfloat16>(
+                         maps[0], maps[1], maps[2], p, s, extra)
+                   : launch_sm100<gmm::kModeGateUp, 1, 1, false, true, __nv_bfloat16>(
+                         maps[0], maps[1], maps[2], p, s, extra);
+  return trans_b ? launch_sm100<gmm::kModeGateUp, 1, 0, false, false, __half>(maps[0], maps[1],
+                                                                             maps[2], p, s, extra)
+                 : launch_sm100<gmm::kModeGateUp, 1, 0, false, true, __half>(maps[0], maps[1],
+                                                                            maps[2], p, s, extra);
 }
 
 // ---------------------------------------------------------------- bounded-wait self-test

@@ -42,11 +42,13 @@ class EPOps:
     unpermute: Callable     # (rows, row_id_map, prob | None (K=1 gather), T, K) -> out [T, d]
     grouped_gemm: Callable  # (A, B [E,N,K], offsets) -> C
     swiglu: Callable = None  # (gate, up) -> silu(gate) * up; None = PyTorch elementwise
+    gate_up: Callable = None  # (A, W_gate, W_up, offsets) -> silu(A.W_gate^T) * (A.W_up^T)
 
 
 def cuda_ops() -> EPOps:
     from . import fused_topk_softmax, grouped_gemm, permute, unpermute
     from .permute_ops import gather_rows
+    from .gate_up_ops import grouped_gemm_swiglu
     from .swiglu_ops import swiglu
 
     def _unpermute(rows, rid, prob, T, K):
@@ -59,7 +61,8 @@ def cuda_ops() -> EPOps:
                  permute=lambda x, idx, E: permute(x, idx, E=E),
                  unpermute=_unpermute,
                  grouped_gemm=lambda a, b, off: grouped_gemm(a, b, off, True),
-                 swiglu=swiglu)
+                 swiglu=swiglu,
+                 gate_up=lambda a, wg, wu, off: grouped_gemm_swiglu(a, wg, wu, off, True))
 
 
 # ------------------------------------------------------------------ index bookkeeping
@@ -143,9 +146,12 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
     recv = all_to_all_rows(permuted[: T * top_k], send_sizes, recv_sizes, group)
     ids = local_expert_ids(recv_counts, world, n_recv)
     grouped, rid2, off2 = ops.permute(recv, ids.unsqueeze(1), el)
-    gate = ops.grouped_gemm(grouped, w_gate_local, off2)
-    up = ops.grouped_gemm(grouped, w_up_local, off2)
-    h = ops.swiglu(gate, up) if ops.swiglu is not None else F.silu(gate) * up
+    if ops.gate_up is not None:
+        h = ops.gate_up(grouped, w_gate_local, w_up_local, off2)
+    else:
+        gate = ops.grouped_gemm(grouped, w_gate_local, off2)
+        up = ops.grouped_gemm(grouped, w_up_local, off2)
+        h = ops.swiglu(gate, up) if ops.swiglu is not None else F.silu(gate) * up
     down = ops.grouped_gemm(h, w_down_local, off2)
     back = ops.unpermute(down, rid2, None, n_recv, 1)
     home = all_to_all_rows(back, recv_sizes, send_sizes, group)
@@ -234,9 +240,9 @@ class _OverlappedExperts(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, permuted, w_gate, w_up, w_down, plan, group):
+        from .gate_up_ops import gmm_gate_up_fwd_raw
         from .grouped_gemm_ops import gmm_fwd_raw
         from .permute_ops import permute_backward, permute_countsort
-        from .swiglu_ops import swiglu_fwd
 
         world = dist.get_world_size(group)
         bounds = plan["bounds"]
@@ -259,9 +265,7 @@ class _OverlappedExperts(torch.autograd.Function):
             cnt = torch.tensor(counts, dtype=torch.int32, device=buf.device)
             ids = local_expert_ids(cnt, world, n)
             grouped, rid2, off2 = permute_countsort(buf, ids.unsqueeze(1), 0, e1 - e0)
-            gate = gmm_fwd_raw(grouped, w_gate[e0:e1], off2, True)
-            up = gmm_fwd_raw(grouped, w_up[e0:e1], off2, True)
-            h = swiglu_fwd(gate, up)
+            gate, up, h = gmm_gate_up_fwd_raw(grouped, w_gate[e0:e1], w_up[e0:e1], off2, True)
             down = gmm_fwd_raw(h, w_down[e0:e1], off2, True)
             back = permute_backward(down, rid2, n, 1)
             combines.append(_a2a_slices(home, sends, back, dparts, group))

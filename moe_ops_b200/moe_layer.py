@@ -5,9 +5,9 @@ Same structure as the reference's example layer SingleGpuMoE (tests/test_moe.py:
     logits  = x @ w_router^T                          (torch GEMM, [T, E])
     w, idx  = fused_topk_softmax(logits, K)
     perm, row_id_map, offsets = permute(x, idx, E=E)
-    gate    = grouped_gemm(perm, w_gate, offsets)     [T*K, H]
-    up      = grouped_gemm(perm, w_up, offsets)       [T*K, H]
-    h       = silu(gate) * up                         (fused SwiGLU kernel)
+    h       = silu(grouped_gemm(perm, w_gate, offsets)) * grouped_gemm(perm, w_up, offsets)
+                                                      [T*K, H]; one launch with the SwiGLU
+                                                      in its epilogue (grouped_gemm_swiglu)
     down    = grouped_gemm(h, w_down, offsets)        [T*K, d]
     out     = unpermute(down, row_id_map, w, T, K)
 
@@ -18,9 +18,9 @@ from __future__ import annotations
 import torch
 
 from .fused_topk_softmax_ops import fused_topk_softmax
+from .gate_up_ops import grouped_gemm_swiglu
 from .grouped_gemm_ops import grouped_gemm
 from .permute_ops import permute
-from .swiglu_ops import swiglu
 from .unpermute_ops import unpermute
 
 
@@ -35,9 +35,7 @@ def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Ten
         logits = logits + router_bias
     weights, indices = fused_topk_softmax(logits, top_k, fp32_routing=fp32_routing)
     permuted, row_id_map, offsets = permute(x, indices, E=E)
-    gate = grouped_gemm(permuted, w_gate, offsets, trans_b=True)
-    up = grouped_gemm(permuted, w_up, offsets, trans_b=True)
-    h = swiglu(gate, up)
+    h = grouped_gemm_swiglu(permuted, w_gate, w_up, offsets, trans_b=True)
     down = grouped_gemm(h, w_down, offsets, trans_b=True)
     return unpermute(down, row_id_map, weights, num_tokens, top_k)
 

@@ -1,0 +1,100 @@
+"""GPU parity of grouped_gemm_swiglu, the fused gate/up GEMM with the SwiGLU epilogue.
+
+The bar is bit equality with the unfused sequence the reference's layer runs
+(tests/test_moe.py:80-82): two grouped GEMMs and the SwiGLU, i.e. this library's
+grouped_gemm and swiglu kernels, whose own parity against the oracle is tested in
+test_grouped_gemm_gpu.py and test_swiglu_gpu.py.  Gradients go through the same kernels,
+so they must match bit for bit too.  One case also checks h against the fp64 oracle.
+"""
+import pytest
+import torch
+
+import moe_ops_b200 as M
+from moe_ops_b200.gate_up_ops import gmm_gate_up_fwd_raw
+from moe_ops_b200.grouped_gemm_ops import gmm_fwd_raw
+from moe_ops_b200.swiglu_ops import swiglu, swiglu_fwd
+from oracle import moe_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(sizes, K, N, dtype, trans_b, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    E, Mt = len(sizes), sum(sizes)
+    A = torch.randn(Mt, K, generator=g).to(dtype).to(dev)
+    shape = (E, N, K) if trans_b else (E, K, N)
+    Wg = (torch.randn(*shape, generator=g) * 0.05).to(dtype).to(dev)
+    Wu = (torch.randn(*shape, generator=g) * 0.05).to(dtype).to(dev)
+    off = torch.zeros(E + 1, dtype=torch.int32)
+    off[1:] = torch.tensor(sizes, dtype=torch.int64).cumsum(0).to(torch.int32)
+    dh = torch.randn(Mt, N, generator=g).to(dtype).to(dev)
+    return A, Wg, Wu, off.to(dev), dh
+
+
+def _check_forward(A, Wg, Wu, off, trans_b):
+    gate, up, h = gmm_gate_up_fwd_raw(A, Wg, Wu, off, trans_b)
+    gate_ref = gmm_fwd_raw(A, Wg, off, trans_b)
+    up_ref = gmm_fwd_raw(A, Wu, off, trans_b)
+    h_ref = swiglu_fwd(gate_ref, up_ref)
+    torch.cuda.synchronize()
+    assert torch.equal(gate, gate_ref), "gate differs from grouped_gemm"
+    assert torch.equal(up, up_ref), "up differs from grouped_gemm"
+    assert torch.equal(h, h_ref), "h differs from grouped_gemm + swiglu"
+    return h
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("trans_b", [True, False])
+def test_forward_bit_equal_ragged(cuda_dev, dtype, trans_b):
+    # Empty experts, tails of 1..127 rows, a column block cut at N=200 (not a multiple of
+    # the 128-column tile), rows spanning several tiles.
+    A, Wg, Wu, off, _ = _case([5, 0, 17, 300, 129, 128, 1, 0, 64, 96], K=192, N=200,
+                              dtype=dtype, trans_b=trans_b, seed=21, dev=cuda_dev)
+    _check_forward(A, Wg, Wu, off, trans_b)
+
+
+def test_forward_bit_equal_cfg4_slice(cuda_dev):
+    # cfg4 shapes (d=4096, H=11008) on 8 experts with 256 +- 16 rows each.
+    g = torch.Generator().manual_seed(22)
+    sizes = (256 + torch.randint(-16, 17, (8,), generator=g)).tolist()
+    A, Wg, Wu, off, _ = _case(sizes, K=4096, N=11008, dtype=torch.bfloat16, trans_b=True,
+                              seed=23, dev=cuda_dev)
+    _check_forward(A, Wg, Wu, off, True)
+
+
+def test_against_fp64_oracle(cuda_dev):
+    A, Wg, Wu, off, _ = _case([40, 0, 170, 90], K=128, N=136, dtype=torch.bfloat16,
+                              trans_b=True, seed=24, dev=cuda_dev)
+    h = M.grouped_gemm_swiglu(A, Wg, Wu, off)
+    Ac, Wgc, Wuc, offc = (t.cpu() for t in (A, Wg, Wu, off))
+    gate = O.gmm_fwd(Ac, Wgc, offc, True)
+    up = O.gmm_fwd(Ac, Wuc, offc, True)
+    h_ref = torch.nn.functional.silu(gate) * up
+    assert O.rel_frobenius(h.cpu(), h_ref) <= 1e-2
+
+
+def test_unaligned_and_fp32_take_the_unfused_kernels(cuda_dev):
+    # K=130 rows are not 16-byte multiples, fp32 has no tensor-core path: both run the
+    # CUDA-core GEMMs and the SwiGLU kernel inside the same entry point.
+    for dtype, K in ((torch.bfloat16, 130), (torch.float32, 96)):
+        A, Wg, Wu, off, _ = _case([10, 0, 70, 33], K=K, N=80, dtype=dtype, trans_b=True,
+                                  seed=25, dev=cuda_dev)
+        _check_forward(A, Wg, Wu, off, True)
+
+
+@pytest.mark.parametrize("trans_b", [True, False])
+def test_backward_bit_equal(cuda_dev, trans_b):
+    A, Wg, Wu, off, dh = _case([33, 0, 250, 128, 7], K=256, N=264, dtype=torch.bfloat16,
+                               trans_b=trans_b, seed=26, dev=cuda_dev)
+    leaves = [t.clone().requires_grad_(True) for t in (A, Wg, Wu)]
+    h = M.grouped_gemm_swiglu(leaves[0], leaves[1], leaves[2], off, trans_b)
+    h.backward(dh)
+    ref = [t.clone().requires_grad_(True) for t in (A, Wg, Wu)]
+    gate = M.grouped_gemm(ref[0], ref[1], off, trans_b)
+    up = M.grouped_gemm(ref[0], ref[2], off, trans_b)
+    h_ref = swiglu(gate, up)
+    h_ref.backward(dh)
+    torch.cuda.synchronize()
+    assert torch.equal(h, h_ref)
+    for name, a, b in zip(("A", "W_gate", "W_up"), leaves, ref):
+        assert torch.equal(a.grad, b.grad), f"grad of {name} differs"
