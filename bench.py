@@ -82,18 +82,23 @@ class ClockSampler:
     background thread while the timed region runs (reads only; changes no setting)."""
 
     REASONS = {  # NVML clocks-event reason bits
-        0x0000000000000008: "hw_slowdown",
-        0x0000000000000040: "hw_thermal_slowdown",
-        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000001: "gpu_idle",
+        0x0000000000000002: "applications_clocks_setting",
         0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000010: "sync_boost",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
         0x0000000000000080: "hw_power_brake_slowdown",
+        0x0000000000000100: "display_clock_setting",
     }
 
-    def __init__(self, gpu_index: int, period_s: float = 0.02):
+    def __init__(self, gpu_index: int, period_s: float = 0.005):
         self.gpu = gpu_index
         self.period = period_s
         self.samples = []
         self.reasons = set()
+        self.bits = 0
         self.smax = None
         self._stop = None
         self._thread = None
@@ -120,6 +125,7 @@ class ClockSampler:
                 try:
                     self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
                     bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.bits |= bits
                     for b, n in self.REASONS.items():
                         if bits & b:
                             self.reasons.add(n)
@@ -137,7 +143,7 @@ class ClockSampler:
         self._thread.join()
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.smax, "reasons": sorted(self.reasons),
-                "samples": len(self.samples)}
+                "reason_bits": hex(self.bits), "samples": len(self.samples)}
 
 
 def _make_inputs(dev, T, d, seed):

@@ -172,6 +172,18 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
                         int64_t m_total, int64_t n, int64_t k, int32_t num_experts, int trans_b,
                         int dtype, void* stream);
 
+/* Backward through the down projection and the SwiGLU of a SwiGLU expert layer, in one
+ * launch: dh = moe_gmm_dgrad(grad_C, B) ([M_total, K], rounded to dtype), then
+ *   grad_gate, grad_up = moe_swiglu_bwd(dh, gate, up)
+ * with gate / up [M_total, K] the forward's projections.  Both results equal the two
+ * separate calls bit for bit; dh itself is never written.  Replaces the down GEMM's dgrad
+ * and the autograd backward of `F.silu(gate) * up` in the reference layer
+ * (tests/test_moe.py:82-83). */
+int moe_gmm_dgrad_swiglu_bwd(const void* grad_C, const void* B, const void* gate, const void* up,
+                             void* grad_gate, void* grad_up, const int32_t* offsets,
+                             int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
+                             int32_t num_experts, int trans_b, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

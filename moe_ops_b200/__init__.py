@@ -23,7 +23,7 @@ from .grouped_gemm_ops import grouped_gemm, supports_tma
 from .permute_ops import permute, permute_backward
 from .unpermute_ops import unpermute, unpermute_forward, unpermute_backward
 from .fused_topk_softmax_ops import fused_topk_softmax
-from .gate_up_ops import grouped_gemm_swiglu
+from .gate_up_ops import grouped_gemm_swiglu, grouped_swiglu_mlp
 
 __all__ = [
     "grouped_gemm",
@@ -34,6 +34,7 @@ __all__ = [
     "unpermute_forward",
     "unpermute_backward",
     "fused_topk_softmax",
-    # beyond the reference's API: gate/up projections with the SwiGLU in one launch
+    # beyond the reference's API: the SwiGLU expert MLP's fused launches
     "grouped_gemm_swiglu",
+    "grouped_swiglu_mlp",
 ]

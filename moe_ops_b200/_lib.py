@@ -49,6 +49,9 @@ SIGNATURES = {
                              _c_int, _c_int, _c_ptr]),
     "moe_gmm_gate_up_fwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32,
                                      _c_i64, _c_i64, _c_i64, _c_i32, _c_int, _c_int, _c_ptr]),
+    "moe_gmm_dgrad_swiglu_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                          _c_i32, _c_i64, _c_i64, _c_i64, _c_i32, _c_int, _c_int,
+                                          _c_ptr]),
     "moe_gmm_dgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
                                _c_int, _c_int, _c_ptr]),
     "moe_gmm_wgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,

@@ -92,7 +92,7 @@ struct Shape {
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA per stage
 };
 
-enum Mode { kModeRows = 0, kModeWgrad = 1, kModeGateUp = 2 };
+enum Mode { kModeRows = 0, kModeWgrad = 1, kModeGateUp = 2, kModeSwiGLUBwd = 3 };
 
 // Output columns one tile covers: a gate/up tile holds 128 gate and 128 up columns in its
 // 256-column accumulator and writes 128 columns of each output.
@@ -129,7 +129,10 @@ struct Params {
   void* out;             // kModeRows: C [m_total, n_out]; kModeWgrad: [E, p_out, n_out];
                          // kModeGateUp: h = silu(gate) * up [m_total, n_out]
   void* out_gate;        // kModeGateUp: gate = A . B_gate^T [m_total, n_out]
-  void* out_up;          // kModeGateUp: up = A . B_up^T [m_total, n_out]
+  void* out_up;          // kModeGateUp: up = A . B_up^T [m_total, n_out];
+                         // kModeSwiGLUBwd: grad of up (`out` holds the grad of gate)
+  const void* in_gate;   // kModeSwiGLUBwd: the forward's gate [m_total, n_out]
+  const void* in_up;     // kModeSwiGLUBwd: the forward's up [m_total, n_out]
 };
 
 struct TileInfo {
@@ -226,6 +229,55 @@ __device__ __forceinline__ bool wait_local(uint32_t bar, uint32_t parity, volati
   return ptx::wait_bounded(bar, parity, abort, kWaitTimeoutNs);
 }
 
+// Stores one 32 x 32 block of 16-bit values held row per lane (`wd`: this lane's row,
+// 16 words) through the warp's 2 KB staging buffer: with a TMA store at (x, y) of `map` when
+// the block's 32 rows are all valid (the store clips columns at the tensor's edge), else
+// with 16-byte stores of the valid rows and columns at dst (element (0, 0) of the block,
+// row pitch `ld` elements).
+template <typename OutT>
+__device__ __forceinline__ void stage_store_block(const uint32_t* wd, uint8_t* cbuf, uint32_t cbuf_u32,
+                                                  int lane, bool use_tma, const CUtensorMap* map,
+                                                  int x, int y, OutT* dst, int64_t ld,
+                                                  int valid_rows, int valid_cols) {
+  if (lane == 0) ptx::bulk_wait_group_read<0>();  // the previous store has read the buffer
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int phys = i ^ ((lane >> 1) & 3);
+    *reinterpret_cast<uint4*>(cbuf + lane * 64 + phys * 16) =
+        make_uint4(wd[i * 4 + 0], wd[i * 4 + 1], wd[i * 4 + 2], wd[i * 4 + 3]);
+  }
+  if (use_tma) {
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      ptx::tma_store_2d(map, cbuf_u32, x, y);
+      ptx::bulk_commit_group();
+    }
+    return;
+  }
+  __syncwarp();
+  const int chunk = lane & 3, cc = chunk * 8;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = (lane >> 2) + i * 8;
+    const int phys = chunk ^ ((rr >> 1) & 3);
+    const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
+    if (rr < valid_rows && cc < valid_cols) *reinterpret_cast<uint4*>(dst + (int64_t)rr * ld + cc) = u;
+  }
+  __syncwarp();
+}
+
+// Packs 32 fp32 values (as bits) into 16 words of 16-bit values.
+template <typename OutT>
+__device__ __forceinline__ void pack32_16b(const uint32_t* v, uint32_t* wd) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 x = pack8_16b<OutT>(&v[i * 8]);
+    wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
+  }
+}
+
 // A_MN / B_MN: the operand is MN-major in global memory (and in shared memory).
 // In kModeRows map_b is 3-D (inner, outer, expert); every other map is 2-D (inner, row).
 // Tensor-map boxes: A 64 x 128 (K-major) or 64 x 64 (MN-major, 2 per CTA); B 64 x B_COLS
@@ -236,7 +288,8 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                  const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_b2,
                  const __grid_constant__ CUtensorMap map_c2, const __grid_constant__ CUtensorMap map_c3,
                  const Params p) {
-  static_assert(MODE != kModeGateUp || CG == 1, "gate/up tiles run on single CTAs");
+  static_assert((MODE != kModeGateUp && MODE != kModeSwiGLUBwd) || CG == 1,
+                "fused-epilogue tiles run on single CTAs");
   using Sh = Shape<CG>;
   constexpr int STAGES = Sh::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -553,71 +606,90 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         const int row_base = ti.row0;
         const bool use_tma = (q + 1) * 32 <= valid_rows;
         const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
-        // Stages one 32 x 32 block of 16-bit words (row per lane) and stores it to `dst`.
-        auto put = [&](const uint32_t* wd, const CUtensorMap* map, OutT* dst, int col) {
-          if (lane == 0) ptx::bulk_wait_group_read<0>();
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int phys = i ^ ((wr_row >> 1) & 3);
-            *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
-                make_uint4(wd[i * 4 + 0], wd[i * 4 + 1], wd[i * 4 + 2], wd[i * 4 + 3]);
-          }
-          if (use_tma) {
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              ptx::tma_store_2d(map, cbuf_u32, n0 + col, row_base + q * 32);
-              ptx::bulk_commit_group();
-            }
-            return;
-          }
-          __syncwarp();
-          const int cc = col + rd_chunk * 8;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rr = rd_row0 + i * 8;
-            const int phys = rd_chunk ^ ((rr >> 1) & 3);
-            const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
-            const int row = q * 32 + rr;
-            if (row < valid_rows && cc < valid_cols)
-              *reinterpret_cast<uint4*>(dst + (int64_t)(row_base + row) * p.n_out + n0 + cc) = u;
-          }
-          __syncwarp();
-        };
-        if (valid_rows > q * 32) {
+        const int vr = min(32, valid_rows - q * 32);
+        OutT* const outs[3] = {static_cast<OutT*>(p.out_gate), static_cast<OutT*>(p.out_up), out};
+        const CUtensorMap* const maps[3] = {&map_c2, &map_c3, &map_c};
+        if (vr > 0) {
           for (int c = 0; c < 2; ++c) {
             const int col = h * 64 + c * 32;
             if (col >= valid_cols) break;
-            uint32_t vg[32], vu[32];
+            uint32_t vg[32], vu[32], wd[16];
             ptx::tmem_ld_32x32b_x32(tbase + col, vg);
             ptx::tmem_ld_32x32b_x32(tbase + BN / 2 + col, vu);
             ptx::tmem_wait_ld();
-            uint32_t wd[16];
+            const int64_t off = (int64_t)(row_base + q * 32) * p.n_out + n0 + col;
+            for (int o = 0; o < 3; ++o) {
+              if (o == 0) pack32_16b<OutT>(vg, wd);
+              else if (o == 1) pack32_16b<OutT>(vu, wd);
+              else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  const float gq = rnd<OutT>(__uint_as_float(vg[i]));
+                  const float uq = rnd<OutT>(__uint_as_float(vu[i]));
+                  vg[i] = __float_as_uint(rnd<OutT>(gq * sigmoid_f32(gq)) * uq);
+                }
+                pack32_16b<OutT>(vg, wd);
+              }
+              stage_store_block<OutT>(wd, cbuf, cbuf_u32, lane, use_tma, maps[o], n0 + col,
+                                      row_base + q * 32, outs[o] + off, p.n_out, vr,
+                                      valid_cols - col);
+            }
+          }
+        }
+      } else if constexpr (MODE == kModeSwiGLUBwd) {
+        // The tile's accumulator is the gradient of h (rows 32q.., columns [128h, 128h+128)
+        // for this warp, four 32-column chunks).  Each lane loads its row's gate and up values,
+        // rounds the gradient to 16 bits as the plain GEMM stores it, and applies the SwiGLU
+        // backward exactly as the SwiGLU backward kernel does, so grad_gate and grad_up equal
+        // dgrad GEMM + SwiGLU backward bit for bit.
+        const int n0 = ti.n_blk * BN;
+        const int valid_cols = min(BN, p.n_out - n0);
+        const int valid_rows = min(BMC, ti.rows);
+        const int row_base = ti.row0;
+        const bool use_tma = (q + 1) * 32 <= valid_rows;
+        const int vr = min(32, valid_rows - q * 32);
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+        const OutT* gin = static_cast<const OutT*>(p.in_gate);
+        const OutT* uin = static_cast<const OutT*>(p.in_up);
+        OutT* dg_out = out;
+        OutT* du_out = static_cast<OutT*>(p.out_up);
+        const bool row_ok = q * 32 + lane < valid_rows;
+        const int64_t my_row = (int64_t)(row_base + q * 32 + lane) * p.n_out;
+        if (vr > 0) {
+          for (int c = 0; c < 4; ++c) {
+            const int col = h * (BN / 2) + c * 32;
+            if (col >= valid_cols) break;
+            uint32_t v[32];
+            ptx::tmem_ld_32x32b_x32(tbase + col, v);
+            uint4 graw[4], uraw[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              const uint4 x = pack8_16b<OutT>(&vg[i * 8]);
-              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
+              const bool ok = row_ok && col + i * 8 < valid_cols;
+              graw[i] = ok ? __ldg(reinterpret_cast<const uint4*>(gin + my_row + n0 + col + i * 8))
+                           : make_uint4(0, 0, 0, 0);
+              uraw[i] = ok ? __ldg(reinterpret_cast<const uint4*>(uin + my_row + n0 + col + i * 8))
+                           : make_uint4(0, 0, 0, 0);
             }
-            put(wd, &map_c2, static_cast<OutT*>(p.out_gate), col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 x = pack8_16b<OutT>(&vu[i * 8]);
-              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
-            }
-            put(wd, &map_c3, static_cast<OutT*>(p.out_up), col);
+            ptx::tmem_wait_ld();
+            const OutT* gv = reinterpret_cast<const OutT*>(graw);
+            const OutT* uv = reinterpret_cast<const OutT*>(uraw);
+            uint32_t vdg[32];
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              const float gq = rnd<OutT>(__uint_as_float(vg[i]));
-              const float uq = rnd<OutT>(__uint_as_float(vu[i]));
-              vg[i] = __float_as_uint(rnd<OutT>(gq * sigmoid_f32(gq)) * uq);
+              float a, b;
+              swiglu_bwd_elem<OutT>(rnd<OutT>(__uint_as_float(v[i])), to_f32(gv[i]), to_f32(uv[i]),
+                                    a, b);
+              vdg[i] = __float_as_uint(a);
+              v[i] = __float_as_uint(b);
             }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const uint4 x = pack8_16b<OutT>(&vg[i * 8]);
-              wd[i * 4 + 0] = x.x; wd[i * 4 + 1] = x.y; wd[i * 4 + 2] = x.z; wd[i * 4 + 3] = x.w;
-            }
-            put(wd, &map_c, out, col);
+            uint32_t wd[16];
+            const int64_t off = (int64_t)(row_base + q * 32) * p.n_out + n0 + col;
+            pack32_16b<OutT>(vdg, wd);
+            stage_store_block<OutT>(wd, cbuf, cbuf_u32, lane, use_tma, &map_c, n0 + col,
+                                    row_base + q * 32, dg_out + off, p.n_out, vr, valid_cols - col);
+            pack32_16b<OutT>(v, wd);
+            stage_store_block<OutT>(wd, cbuf, cbuf_u32, lane, use_tma, &map_c3, n0 + col,
+                                    row_base + q * 32, du_out + off, p.n_out, vr, valid_cols - col);
           }
         }
       } else {

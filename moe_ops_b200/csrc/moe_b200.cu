@@ -172,15 +172,36 @@ static int launch_fmt_cg(int dtype, int cg, const CUtensorMap& ma, const CUtenso
                  : launch_sm100<MODE, 1, 0, A_MN, B_MN, __half>(ma, mb, mc, p, stream);
 }
 
+// SwiGLU backward applied to a row-mode product D (the gradient of h = silu(gate) * up):
+// C receives the gradient of gate, grad_up that of up.
+struct SwiGLUBwdArgs {
+  const void* gate;
+  const void* up;
+  void* grad_up;
+};
+
+static int swiglu_bwd_launch(const void* grad_out, const void* gate, const void* up,
+                             void* grad_gate, void* grad_up, int64_t n, int dtype,
+                             cudaStream_t s);
+
 // Row mode (forward / dgrad): C[m_total, n_out] = A[m_total, k_red] . op(B[g]).
 // b_mn: B[g] stored [k_red, n_out] (MN-major) instead of [n_out, k_red].
+// sw: also apply the SwiGLU backward to the product (C becomes the gate gradient).
 static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offsets, int plus_one,
                     int64_t m_total, int64_t n_out, int64_t k_red, int E, bool b_mn, int dtype,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const SwiGLUBwdArgs* sw = nullptr) {
   if (m_total == 0 || n_out == 0) return MOE_OK;
   const bool tc = dtype != MOE_F32 && k_red % 8 == 0 && n_out % 8 == 0 && E <= gmm::kMaxGroups &&
                   aligned16(A) && aligned16(B) && aligned16(C) && m_total < (1ll << 31) &&
-                  n_out < (1ll << 31) && k_red < (1ll << 31);
+                  n_out < (1ll << 31) && k_red < (1ll << 31) &&
+                  (!sw || (aligned16(sw->gate) && aligned16(sw->up) && aligned16(sw->grad_up)));
+  if (sw && (!tc || k_red == 0)) {
+    // The product into C, then the SwiGLU backward in place (each element is read before
+    // the same thread writes it).
+    int rc = gmm_rows(A, B, C, offsets, plus_one, m_total, n_out, k_red, E, b_mn, dtype, stream);
+    if (rc) return rc;
+    return swiglu_bwd_launch(C, sw->gate, sw->up, C, sw->grad_up, m_total * n_out, dtype, stream);
+  }
   if (!tc || k_red == 0) {
     if (k_red == 0) {
       MOE_CUDA_CHECK(cudaMemsetAsync(C, 0, (size_t)m_total * n_out * dtype_size(dtype), stream));
@@ -208,7 +229,7 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   }
   // Single-CTA tiles: measured on B200 against SM pairs (with half tail tiles) for 256 to
   // 2048 rows per expert at d=4096 / H=11008 shapes, they run 3-15 % faster in this mode.
-  const int cg = pick_cg(1);
+  const int cg = sw ? 1 : pick_cg(1);
   const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
@@ -229,12 +250,14 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     int rc = make_map(&mb, B, dtype, 3, dims, box);
     if (rc) return rc;
   }
-  CUtensorMap mc;  // output, 32 x 32 boxes in the epilogue's 64-byte swizzle
+  CUtensorMap mc, mc_up;  // outputs, 32 x 32 boxes in the epilogue's 64-byte swizzle
   {
     const uint64_t dims[2] = {(uint64_t)n_out, (uint64_t)m_total};
     const uint32_t box[2] = {32, 32};
     int rc = make_map(&mc, C, dtype, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc) return rc;
+    if (sw && (rc = make_map(&mc_up, sw->grad_up, dtype, 2, dims, box, CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
   }
   gmm::Params p = {};
   p.offsets = offsets;
@@ -245,6 +268,18 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   p.p_out = 0;
   p.k_red = (int)k_red;
   p.out = C;
+  if (sw) {
+    p.out_up = sw->grad_up;
+    p.in_gate = sw->gate;
+    p.in_up = sw->up;
+    const CUtensorMap extra[3] = {mb, mc, mc_up};
+    constexpr int M3 = gmm::kModeSwiGLUBwd;
+    if (dtype == MOE_BF16)
+      return b_mn ? launch_sm100<M3, 1, 1, false, true, __nv_bfloat16>(ma, mb, mc, p, stream, extra)
+                  : launch_sm100<M3, 1, 1, false, false, __nv_bfloat16>(ma, mb, mc, p, stream, extra);
+    return b_mn ? launch_sm100<M3, 1, 0, false, true, __half>(ma, mb, mc, p, stream, extra)
+                : launch_sm100<M3, 1, 0, false, false, __half>(ma, mb, mc, p, stream, extra);
+  }
   return b_mn ? launch_fmt_cg<gmm::kModeRows, false, true>(dtype, cg, ma, mb, mc, p, stream)
               : launch_fmt_cg<gmm::kModeRows, false, false>(dtype, cg, ma, mb, mc, p, stream);
 }
@@ -334,6 +369,27 @@ static PermuteWorkspace permute_ws(int64_t T, int K, int E) {
   w.cnt_bytes = (size_t)w.num_tiles * E * sizeof(int32_t);
   w.total_bytes = w.cnt_bytes + 16;
   return w;
+}
+
+// Grid of the grid-stride elementwise kernels: up to 8 blocks of 256 threads per SM.
+static unsigned elementwise_grid(int64_t n, int per_thread) {
+  const int64_t blocks = (n / per_thread + 255) / 256;
+  const int64_t cap = (int64_t)num_sms(current_device()) * 8;
+  return (unsigned)std::max<int64_t>(1, std::min(blocks, cap));
+}
+
+static int swiglu_bwd_launch(const void* grad_out, const void* gate, const void* up,
+                             void* grad_gate, void* grad_up, int64_t n, int dtype,
+                             cudaStream_t s) {
+  if (n == 0) return MOE_OK;
+  const unsigned grid = elementwise_grid(n, 16 / dtype_size(dtype));
+  switch (dtype) {
+    case MOE_F32: swiglu_bwd_kernel<float><<<grid, 256, 0, s>>>((const float*)grad_out, (const float*)gate, (const float*)up, (float*)grad_gate, (float*)grad_up, n); break;
+    case MOE_F16: swiglu_bwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)grad_out, (const __half*)gate, (const __half*)up, (__half*)grad_gate, (__half*)grad_up, n); break;
+    default: swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)grad_out, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)up, (__nv_bfloat16*)grad_gate, (__nv_bfloat16*)grad_up, n);
+  }
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
 }
 
 }  // namespace moe
@@ -451,12 +507,6 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   return MOE_OK;
 }
 
-static unsigned elementwise_grid(int64_t n, int per_thread) {
-  const int64_t blocks = (n / per_thread + 255) / 256;
-  const int64_t cap = (int64_t)num_sms(current_device()) * 8;
-  return (unsigned)std::max<int64_t>(1, std::min(blocks, cap));
-}
-
 int moe_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream) {
   MOE_REQUIRE(dtype == MOE_BF16 || dtype == MOE_F16 || dtype == MOE_F32, "swiglu: bad dtype %d", dtype);
   MOE_REQUIRE(n >= 0, "swiglu: negative size");
@@ -480,16 +530,7 @@ int moe_swiglu_bwd(const void* grad_out, const void* gate, const void* up, void*
   MOE_REQUIRE(aligned16(grad_out) && aligned16(gate) && aligned16(up) && aligned16(grad_gate) &&
                   aligned16(grad_up),
               "swiglu_bwd: pointers must be 16-byte aligned");
-  if (n == 0) return MOE_OK;
-  cudaStream_t s = (cudaStream_t)stream;
-  const unsigned grid = elementwise_grid(n, 16 / dtype_size(dtype));
-  switch (dtype) {
-    case MOE_F32: swiglu_bwd_kernel<float><<<grid, 256, 0, s>>>((const float*)grad_out, (const float*)gate, (const float*)up, (float*)grad_gate, (float*)grad_up, n); break;
-    case MOE_F16: swiglu_bwd_kernel<__half><<<grid, 256, 0, s>>>((const __half*)grad_out, (const __half*)gate, (const __half*)up, (__half*)grad_gate, (__half*)grad_up, n); break;
-    default: swiglu_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)grad_out, (const __nv_bfloat16*)gate, (const __nv_bfloat16*)up, (__nv_bfloat16*)grad_gate, (__nv_bfloat16*)grad_up, n);
-  }
-  MOE_LAUNCH_CHECK();
-  return MOE_OK;
+  return swiglu_bwd_launch(grad_out, gate, up, grad_gate, grad_up, n, dtype, (cudaStream_t)stream);
 }
 
 int moe_scatter_rows(const void* input, int dtype, const int32_t* row_id_map, int64_t num_tokens,
@@ -709,6 +750,22 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
                                                                              maps[2], p, s, extra)
                  : launch_sm100<gmm::kModeGateUp, 1, 0, false, true, __half>(maps[0], maps[1],
                                                                             maps[2], p, s, extra);
+}
+
+int moe_gmm_dgrad_swiglu_bwd(const void* grad_C, const void* B, const void* gate, const void* up,
+                             void* grad_gate, void* grad_up, const int32_t* offsets,
+                             int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
+                             int32_t E, int trans_b, int dtype, void* stream) {
+  int rc = check_gmm_args(grad_C, B, grad_gate, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  MOE_REQUIRE((gate && up && grad_up) || m_total == 0 || E == 0, "gmm_dgrad_swiglu_bwd: NULL operand");
+  MOE_REQUIRE(aligned16(gate) && aligned16(up) && aligned16(grad_gate) && aligned16(grad_up),
+              "gmm_dgrad_swiglu_bwd: gate, up and the gradients must be 16-byte aligned");
+  if (E == 0) return MOE_OK;
+  const SwiGLUBwdArgs sw = {gate, up, grad_up};
+  // As moe_gmm_dgrad: the product is [M, k] = grad_C [M, n] . B'[e].
+  return gmm_rows(grad_C, B, grad_gate, offsets, num_offsets == E + 1, m_total, k, n, E,
+                  trans_b != 0, dtype, (cudaStream_t)stream, &sw);
 }
 
 // ---------------------------------------------------------------- bounded-wait self-test

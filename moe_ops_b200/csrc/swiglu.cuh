@@ -47,6 +47,17 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ g
   }
 }
 
+// Backward of one element: d = upstream gradient, x = gate, uu = up (all as stored,
+// widened to fp32); returns the unrounded fp32 gradients of gate and up.
+template <typename T>
+__device__ __forceinline__ void swiglu_bwd_elem(float d, float x, float uu, float& dgo, float& duo) {
+  const float sg = sigmoid_f32(x);
+  const float s = rnd<T>(x * sg);
+  duo = d * s;
+  const float ds = rnd<T>(d * uu);
+  dgo = ds * (sg * (1.f + x * (1.f - sg)));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ g,
                                                          const T* __restrict__ u, T* __restrict__ dg,
@@ -54,13 +65,6 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ d
   constexpr int V = 16 / sizeof(T);
   const int64_t nv = n / V;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  auto one = [](float d, float x, float uu, float& dgo, float& duo) {
-    const float sg = sigmoid_f32(x);
-    const float s = rnd<T>(x * sg);
-    duo = d * s;
-    const float ds = rnd<T>(d * uu);
-    dgo = ds * (sg * (1.f + x * (1.f - sg)));
-  };
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += stride) {
     const uint4 dv = reinterpret_cast<const uint4*>(dh)[i];
     const uint4 gv = reinterpret_cast<const uint4*>(g)[i];
@@ -74,7 +78,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ d
 #pragma unroll
     for (int j = 0; j < V; ++j) {
       float a, b;
-      one(to_f32(dp[j]), to_f32(gp[j]), to_f32(up[j]), a, b);
+      swiglu_bwd_elem<T>(to_f32(dp[j]), to_f32(gp[j]), to_f32(up[j]), a, b);
       gop[j] = from_f32<T>(a);
       uop[j] = from_f32<T>(b);
     }
@@ -83,7 +87,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ d
   }
   for (int64_t i = nv * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     float a, b;
-    one(to_f32(dh[i]), to_f32(g[i]), to_f32(u[i]), a, b);
+    swiglu_bwd_elem<T>(to_f32(dh[i]), to_f32(g[i]), to_f32(u[i]), a, b);
     dg[i] = from_f32<T>(a);
     du[i] = from_f32<T>(b);
   }

@@ -42,13 +42,15 @@ class EPOps:
     unpermute: Callable     # (rows, row_id_map, prob | None (K=1 gather), T, K) -> out [T, d]
     grouped_gemm: Callable  # (A, B [E,N,K], offsets) -> C
     swiglu: Callable = None  # (gate, up) -> silu(gate) * up; None = PyTorch elementwise
-    gate_up: Callable = None  # (A, W_gate, W_up, offsets) -> silu(A.W_gate^T) * (A.W_up^T)
+    # (A, W_gate, W_up, W_down, offsets) -> the SwiGLU expert MLP in fused launches; None =
+    # grouped_gemm / swiglu above
+    expert_mlp: Callable = None
 
 
 def cuda_ops() -> EPOps:
     from . import fused_topk_softmax, grouped_gemm, permute, unpermute
     from .permute_ops import gather_rows
-    from .gate_up_ops import grouped_gemm_swiglu
+    from .gate_up_ops import grouped_swiglu_mlp
     from .swiglu_ops import swiglu
 
     def _unpermute(rows, rid, prob, T, K):
@@ -62,7 +64,7 @@ def cuda_ops() -> EPOps:
                  unpermute=_unpermute,
                  grouped_gemm=lambda a, b, off: grouped_gemm(a, b, off, True),
                  swiglu=swiglu,
-                 gate_up=lambda a, wg, wu, off: grouped_gemm_swiglu(a, wg, wu, off, True))
+                 expert_mlp=lambda a, wg, wu, wd, off: grouped_swiglu_mlp(a, wg, wu, wd, off, True))
 
 
 # ------------------------------------------------------------------ index bookkeeping
@@ -146,13 +148,13 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
     recv = all_to_all_rows(permuted[: T * top_k], send_sizes, recv_sizes, group)
     ids = local_expert_ids(recv_counts, world, n_recv)
     grouped, rid2, off2 = ops.permute(recv, ids.unsqueeze(1), el)
-    if ops.gate_up is not None:
-        h = ops.gate_up(grouped, w_gate_local, w_up_local, off2)
+    if ops.expert_mlp is not None:
+        down = ops.expert_mlp(grouped, w_gate_local, w_up_local, w_down_local, off2)
     else:
         gate = ops.grouped_gemm(grouped, w_gate_local, off2)
         up = ops.grouped_gemm(grouped, w_up_local, off2)
         h = ops.swiglu(gate, up) if ops.swiglu is not None else F.silu(gate) * up
-    down = ops.grouped_gemm(h, w_down_local, off2)
+        down = ops.grouped_gemm(h, w_down_local, off2)
     back = ops.unpermute(down, rid2, None, n_recv, 1)
     home = all_to_all_rows(back, recv_sizes, send_sizes, group)
     return ops.unpermute(home, rid, weights, T, top_k)
@@ -279,9 +281,9 @@ class _OverlappedExperts(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_home):
+        from .gate_up_ops import gmm_dgrad_swiglu_bwd_raw
         from .grouped_gemm_ops import _gmm_call, gmm_dgrad_raw
         from .permute_ops import permute_backward
-        from .swiglu_ops import swiglu_bwd
 
         w_gate, w_up, w_down = ctx.saved_tensors
         plan, group = ctx.plan, ctx.group
@@ -308,10 +310,9 @@ class _OverlappedExperts(torch.autograd.Function):
             n = buf.shape[0]
             el = e1 - e0
             g_down_rows = torch.ops.moeb200.scatter_rows(buf, rid2, n, 1)  # recv -> grouped order
-            dh = gmm_dgrad_raw(g_down_rows, w_down[e0:e1], off2, True)
+            dgate, dup = gmm_dgrad_swiglu_bwd_raw(g_down_rows, w_down[e0:e1], gate, up, off2, True)
             _gmm_call("moe_gmm_wgrad", h, g_down_rows, g_down[e0:e1], off2, n, w_down.shape[1],
                       w_down.shape[2], el, True)
-            dgate, dup = swiglu_bwd(dh, gate, up)
             dgrouped = gmm_dgrad_raw(dgate, w_gate[e0:e1], off2, True)
             dgrouped += gmm_dgrad_raw(dup, w_up[e0:e1], off2, True)
             _gmm_call("moe_gmm_wgrad", grouped, dgate, g_gate[e0:e1], off2, n, w_gate.shape[1],

@@ -1,4 +1,5 @@
-"""Gate and up projections of a SwiGLU expert layer, fused with the SwiGLU.
+"""The SwiGLU expert MLP's fused launches: gate/up projections with the SwiGLU, and the
+down projection's dgrad with the SwiGLU backward.
 
 The reference's example layer runs two grouped GEMMs and a PyTorch SwiGLU
 (tests/test_moe.py:80-82):
@@ -10,8 +11,14 @@ The reference's example layer runs two grouped GEMMs and a PyTorch SwiGLU
 ``grouped_gemm_swiglu(permuted, w_gate, w_up, offsets)`` returns the same ``h`` from one
 tensor-core launch: each tile accumulates 128 gate and 128 up columns of the same rows, and
 its epilogue writes gate, up (kept for the backward) and h.  The three outputs equal the
-unfused sequence bit for bit (same accumulation order, same rounding steps).  The backward
+unfused sequence bit for bit (same accumulation order, same rounding steps).  Its backward
 is the unfused one: SwiGLU backward, two dgrad GEMMs summed, two wgrad GEMMs.
+
+``grouped_swiglu_mlp(permuted, w_gate, w_up, w_down, offsets)`` is the whole expert MLP,
+``grouped_gemm(h, w_down)`` on top of the above.  Its backward runs the down projection's
+dgrad with the SwiGLU backward in the epilogue (``gmm_dgrad_swiglu_bwd_raw``): the gradient
+of h is never written, and grad_gate / grad_up equal dgrad GEMM + SwiGLU backward bit for
+bit.
 """
 from __future__ import annotations
 
@@ -19,7 +26,7 @@ import torch
 
 from . import _lib
 from . import swiglu_ops  # noqa: F401  (registers moeb200::swiglu_bwd)
-from .grouped_gemm_ops import _norm_offsets, gmm_bwd_B_raw, gmm_dgrad_raw
+from .grouped_gemm_ops import _norm_offsets, gmm_bwd_B_raw, gmm_dgrad_raw, gmm_fwd_raw
 
 _NS = "moeb200"
 
@@ -70,6 +77,62 @@ def _(A, B_gate, B_up, offsets, trans_b=True):
     return (A.new_empty(shape), A.new_empty(shape), A.new_empty(shape))
 
 
+@torch.library.custom_op(f"{_NS}::gmm_dgrad_swiglu_bwd_raw", mutates_args=())
+def gmm_dgrad_swiglu_bwd_raw(grad_output: torch.Tensor, B: torch.Tensor, gate: torch.Tensor,
+                             up: torch.Tensor, offsets: torch.Tensor,
+                             trans_b: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """(grad_gate, grad_up) = swiglu_bwd(gmm_dgrad_raw(grad_output, B), gate, up) in one
+    launch; gate / up are the forward's projections (the shape of the dgrad result)."""
+    assert grad_output.dtype == B.dtype == gate.dtype == up.dtype, "operands must share one dtype"
+    _lib.require_cuda(grad_output, B, gate, up, offsets)
+    grad_output, B = grad_output.contiguous(), B.contiguous()
+    gate, up = gate.contiguous(), up.contiguous()
+    total, N = grad_output.shape
+    E = B.shape[0]
+    K = B.shape[2] if trans_b else B.shape[1]
+    assert gate.shape == up.shape == (total, K), "gate / up must match the dgrad result"
+    offsets = _norm_offsets(offsets, E)
+    grad_gate = torch.empty_like(gate)
+    grad_up = torch.empty_like(up)
+    lib = _lib.load()
+    timing = _lib.gemm_timing
+    with torch.cuda.device(grad_output.device):
+        if timing is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        st = lib.moe_gmm_dgrad_swiglu_bwd(
+            _lib.ptr(grad_output), _lib.ptr(B), _lib.ptr(gate), _lib.ptr(up), _lib.ptr(grad_gate),
+            _lib.ptr(grad_up), _lib.ptr(offsets), offsets.numel(), total, N, K, E,
+            int(bool(trans_b)), _lib.dtype_code(grad_output.dtype), _lib.stream_of(grad_output))
+        if timing is not None:
+            ev1.record()
+            es = grad_output.element_size()
+            timing.append(("moe_gmm_dgrad_swiglu_bwd", ev0, ev1, 2.0 * total * N * K,
+                           E * N * K * es + total * N * es + 2 * total * K * es,
+                           2 * total * K * es))
+    _lib.check(st, "moe_gmm_dgrad_swiglu_bwd")
+    _lib.count_launches(1)
+    return grad_gate, grad_up
+
+
+@gmm_dgrad_swiglu_bwd_raw.register_fake
+def _(grad_output, B, gate, up, offsets, trans_b=True):
+    return torch.empty_like(gate), torch.empty_like(up)
+
+
+def _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b, needs):
+    grad_A = grad_g = grad_u = None
+    if needs[0]:
+        grad_A = gmm_dgrad_raw(dgate, B_gate, offsets, trans_b)
+        grad_A += gmm_dgrad_raw(dup, B_up, offsets, trans_b)
+    if needs[1]:
+        grad_g = gmm_bwd_B_raw(A, B_gate, offsets, dgate, trans_b)
+    if needs[2]:
+        grad_u = gmm_bwd_B_raw(A, B_up, offsets, dup, trans_b)
+    return grad_A, grad_g, grad_u
+
+
 class GroupedGateUpSwiGLU(torch.autograd.Function):
     @staticmethod
     def forward(ctx, A, B_gate, B_up, offsets, trans_b):
@@ -83,15 +146,9 @@ class GroupedGateUpSwiGLU(torch.autograd.Function):
         A, B_gate, B_up, offsets, gate, up = ctx.saved_tensors
         trans_b = ctx.trans_b
         dgate, dup = torch.ops.moeb200.swiglu_bwd(grad_h, gate, up)
-        grad_A = grad_g = grad_u = None
-        if ctx.needs_input_grad[0]:
-            grad_A = gmm_dgrad_raw(dgate, B_gate, offsets, trans_b)
-            grad_A += gmm_dgrad_raw(dup, B_up, offsets, trans_b)
-        if ctx.needs_input_grad[1]:
-            grad_g = gmm_bwd_B_raw(A, B_gate, offsets, dgate, trans_b)
-        if ctx.needs_input_grad[2]:
-            grad_u = gmm_bwd_B_raw(A, B_up, offsets, dup, trans_b)
-        return grad_A, grad_g, grad_u, None, None
+        grads = _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b,
+                                  ctx.needs_input_grad[:3])
+        return (*grads, None, None)
 
 
 def grouped_gemm_swiglu(A: torch.Tensor, B_gate: torch.Tensor, B_up: torch.Tensor,
@@ -101,4 +158,34 @@ def grouped_gemm_swiglu(A: torch.Tensor, B_gate: torch.Tensor, B_up: torch.Tenso
     return GroupedGateUpSwiGLU.apply(A, B_gate, B_up, offsets, trans_b)
 
 
-__all__ = ["grouped_gemm_swiglu", "gmm_gate_up_fwd_raw"]
+class GroupedSwiGLUMLP(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, A, B_gate, B_up, B_down, offsets, trans_b):
+        gate, up, h = torch.ops.moeb200.gmm_gate_up_fwd_raw(A, B_gate, B_up, offsets, trans_b)
+        out = gmm_fwd_raw(h, B_down, offsets, trans_b)
+        ctx.save_for_backward(A, B_gate, B_up, B_down, offsets, gate, up, h)
+        ctx.trans_b = trans_b
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        A, B_gate, B_up, B_down, offsets, gate, up, h = ctx.saved_tensors
+        trans_b = ctx.trans_b
+        grad_out = grad_out.contiguous()
+        dgate, dup = gmm_dgrad_swiglu_bwd_raw(grad_out, B_down, gate, up, offsets, trans_b)
+        grad_d = gmm_bwd_B_raw(h, B_down, offsets, grad_out, trans_b) if ctx.needs_input_grad[3] else None
+        grads = _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b,
+                                  ctx.needs_input_grad[:3])
+        return (*grads, grad_d, None, None)
+
+
+def grouped_swiglu_mlp(A: torch.Tensor, B_gate: torch.Tensor, B_up: torch.Tensor,
+                       B_down: torch.Tensor, offsets: torch.Tensor,
+                       trans_b: bool = True) -> torch.Tensor:
+    """grouped_gemm(silu(grouped_gemm(A, B_gate)) * grouped_gemm(A, B_up), B_down),
+    differentiable: the SwiGLU expert MLP over grouped rows with both fused launches."""
+    return GroupedSwiGLUMLP.apply(A, B_gate, B_up, B_down, offsets, trans_b)
+
+
+__all__ = ["grouped_gemm_swiglu", "grouped_swiglu_mlp", "gmm_gate_up_fwd_raw",
+           "gmm_dgrad_swiglu_bwd_raw"]

@@ -6,9 +6,9 @@ Same structure as the reference's example layer SingleGpuMoE (tests/test_moe.py:
     w, idx  = fused_topk_softmax(logits, K)
     perm, row_id_map, offsets = permute(x, idx, E=E)
     h       = silu(grouped_gemm(perm, w_gate, offsets)) * grouped_gemm(perm, w_up, offsets)
-                                                      [T*K, H]; one launch with the SwiGLU
-                                                      in its epilogue (grouped_gemm_swiglu)
     down    = grouped_gemm(h, w_down, offsets)        [T*K, d]
+              (grouped_swiglu_mlp: gate/up + SwiGLU in one launch; in the backward the down
+              projection's dgrad carries the SwiGLU backward in its epilogue)
     out     = unpermute(down, row_id_map, w, T, K)
 
 Weights: w_router [E, d], w_gate / w_up [E, H, d], w_down [E, d, H] (trans_b=True layout).
@@ -18,8 +18,7 @@ from __future__ import annotations
 import torch
 
 from .fused_topk_softmax_ops import fused_topk_softmax
-from .gate_up_ops import grouped_gemm_swiglu
-from .grouped_gemm_ops import grouped_gemm
+from .gate_up_ops import grouped_swiglu_mlp
 from .permute_ops import permute
 from .unpermute_ops import unpermute
 
@@ -35,8 +34,7 @@ def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Ten
         logits = logits + router_bias
     weights, indices = fused_topk_softmax(logits, top_k, fp32_routing=fp32_routing)
     permuted, row_id_map, offsets = permute(x, indices, E=E)
-    h = grouped_gemm_swiglu(permuted, w_gate, w_up, offsets, trans_b=True)
-    down = grouped_gemm(h, w_down, offsets, trans_b=True)
+    down = grouped_swiglu_mlp(permuted, w_gate, w_up, w_down, offsets, trans_b=True)
     return unpermute(down, row_id_map, weights, num_tokens, top_k)
 
 

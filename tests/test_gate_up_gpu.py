@@ -98,3 +98,85 @@ def test_backward_bit_equal(cuda_dev, trans_b):
     assert torch.equal(h, h_ref)
     for name, a, b in zip(("A", "W_gate", "W_up"), leaves, ref):
         assert torch.equal(a.grad, b.grad), f"grad of {name} differs"
+
+
+# ------------------------------------------------------------------ down dgrad + SwiGLU backward
+
+
+def _bwd_case(sizes, H, d, dtype, trans_b, seed, dev):
+    g = torch.Generator().manual_seed(seed)
+    E, Mt = len(sizes), sum(sizes)
+    gy = torch.randn(Mt, d, generator=g).to(dtype).to(dev)  # gradient of the down output
+    Wd = (torch.randn(*((E, d, H) if trans_b else (E, H, d)), generator=g) * 0.05).to(dtype).to(dev)
+    gate = torch.randn(Mt, H, generator=g).to(dtype).to(dev)
+    up = torch.randn(Mt, H, generator=g).to(dtype).to(dev)
+    off = torch.zeros(E + 1, dtype=torch.int32)
+    off[1:] = torch.tensor(sizes, dtype=torch.int64).cumsum(0).to(torch.int32)
+    return gy, Wd, gate, up, off.to(dev)
+
+
+def _check_dgrad_swiglu(gy, Wd, gate, up, off, trans_b):
+    from moe_ops_b200.gate_up_ops import gmm_dgrad_swiglu_bwd_raw
+    from moe_ops_b200.grouped_gemm_ops import gmm_dgrad_raw
+    from moe_ops_b200.swiglu_ops import swiglu_bwd
+    dg, du = gmm_dgrad_swiglu_bwd_raw(gy, Wd, gate, up, off, trans_b)
+    dh = gmm_dgrad_raw(gy, Wd, off, trans_b)
+    dg_ref, du_ref = swiglu_bwd(dh, gate, up)
+    torch.cuda.synchronize()
+    assert torch.equal(dg, dg_ref), "grad_gate differs from dgrad + swiglu_bwd"
+    assert torch.equal(du, du_ref), "grad_up differs from dgrad + swiglu_bwd"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("trans_b", [True, False])
+def test_dgrad_swiglu_bwd_bit_equal_ragged(cuda_dev, dtype, trans_b):
+    # H=264 cuts the last 256-column tile; tails of 1..127 rows; empty experts.
+    case = _bwd_case([5, 0, 17, 300, 129, 128, 1, 0, 64, 96], H=264, d=192, dtype=dtype,
+                     trans_b=trans_b, seed=31, dev=cuda_dev)
+    _check_dgrad_swiglu(*case, trans_b)
+
+
+def test_dgrad_swiglu_bwd_bit_equal_cfg4_slice(cuda_dev):
+    g = torch.Generator().manual_seed(32)
+    sizes = (256 + torch.randint(-16, 17, (8,), generator=g)).tolist()
+    case = _bwd_case(sizes, H=11008, d=4096, dtype=torch.bfloat16, trans_b=True, seed=33,
+                     dev=cuda_dev)
+    _check_dgrad_swiglu(*case, True)
+
+
+def test_dgrad_swiglu_bwd_unfused_paths(cuda_dev):
+    # H=130 (rows not 16-byte multiples) and fp32 run the CUDA-core GEMM and the SwiGLU
+    # backward kernel in place inside the same entry point.
+    for dtype, H in ((torch.bfloat16, 130), (torch.float32, 96)):
+        case = _bwd_case([10, 0, 70, 33], H=H, d=64, dtype=dtype, trans_b=True, seed=34,
+                         dev=cuda_dev)
+        _check_dgrad_swiglu(*case, True)
+
+
+@pytest.mark.parametrize("trans_b", [True, False])
+def test_mlp_backward_bit_equal(cuda_dev, trans_b):
+    # The whole expert MLP against the unfused autograd chain the reference's layer uses.
+    g = torch.Generator().manual_seed(35)
+    sizes, d, H = [33, 0, 250, 128, 7], 192, 264
+    E, Mt = len(sizes), sum(sizes)
+    A = torch.randn(Mt, d, generator=g).to(torch.bfloat16).to(cuda_dev)
+    shape_gu = (E, H, d) if trans_b else (E, d, H)
+    shape_d = (E, d, H) if trans_b else (E, H, d)
+    Wg = (torch.randn(*shape_gu, generator=g) * 0.05).to(torch.bfloat16).to(cuda_dev)
+    Wu = (torch.randn(*shape_gu, generator=g) * 0.05).to(torch.bfloat16).to(cuda_dev)
+    Wd = (torch.randn(*shape_d, generator=g) * 0.05).to(torch.bfloat16).to(cuda_dev)
+    gy = torch.randn(Mt, d, generator=g).to(torch.bfloat16).to(cuda_dev)
+    off = torch.zeros(E + 1, dtype=torch.int32)
+    off[1:] = torch.tensor(sizes, dtype=torch.int64).cumsum(0).to(torch.int32)
+    off = off.to(cuda_dev)
+    fused = [t.clone().requires_grad_(True) for t in (A, Wg, Wu, Wd)]
+    out = M.grouped_swiglu_mlp(*fused, off, trans_b)
+    out.backward(gy)
+    ref = [t.clone().requires_grad_(True) for t in (A, Wg, Wu, Wd)]
+    h_ref = swiglu(M.grouped_gemm(ref[0], ref[1], off, trans_b), M.grouped_gemm(ref[0], ref[2], off, trans_b))
+    out_ref = M.grouped_gemm(h_ref, ref[3], off, trans_b)
+    out_ref.backward(gy)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out_ref)
+    for name, a, b in zip(("A", "W_gate", "W_up", "W_down"), fused, ref):
+        assert torch.equal(a.grad, b.grad), f"grad of {name} differs"
