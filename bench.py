@@ -167,6 +167,12 @@ def run_ours(args):
     cfg = CONFIGS[args.config]
     d, E, K, H = cfg["d_model"], cfg["experts"], cfg["top_k"], cfg["hidden"]
     T = cfg["tokens"] // world if cfg["global_tokens"] else cfg["tokens"]
+    if args.experts and args.experts != E:
+        # A slice of the config for profiling: fewer experts, tokens scaled to keep the
+        # rows per expert.  Not the headline workload; the JSON line says so.
+        T = T * args.experts // E
+        E = args.experts
+        cfg = dict(cfg, workload=cfg["workload"] + f" [slice: E={E}, T={T}]")
     router_std = cfg["router_std"] or d ** -0.5  # None: logits ~ N(0, 1)
 
     if world == 1:
@@ -438,7 +444,7 @@ def run_case(args):
             E, K, N = 16, 4096, 4096
             sizes = [1024] * 16
         else:
-            E, K, N = args.experts, 4096, 11008
+            E, K, N = args.experts or 64, 4096, 11008
             cpu_g = torch.Generator().manual_seed(0)
             sizes = torch.bincount(torch.randint(0, E, (args.rows_per_expert * E,), generator=cpu_g),
                                    minlength=E).tolist()
@@ -496,7 +502,9 @@ def main():
                     help="layer workload: cfg4 (headline, default) or cfg5")
     ap.add_argument("--case", default="layer",
                     help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing")
-    ap.add_argument("--experts", type=int, default=64, help="gmm-* cases: experts (cfg4 shapes)")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="gmm-* cases: experts (cfg4 shapes, default 64); layer case: run a "
+                         "slice of the config with this many experts (profiling)")
     ap.add_argument("--cfg2", action="store_true", help="gmm-* cases: BASELINE config 2 shapes")
     ap.add_argument("--rows-per-expert", type=int, default=256, help="gmm-* cases: mean rows")
     ap.add_argument("--gpus", type=int, default=1)

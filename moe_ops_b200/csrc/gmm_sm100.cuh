@@ -592,6 +592,23 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
       const int buf = acc & 1;
       const uint32_t acc_phase = (acc >> 1) & 1;
+      if constexpr (MODE == kModeSwiGLUBwd) {
+        // While this tile's main loop runs, pull the gate / up values its epilogue will
+        // read into L2: this lane's row, the warp's 128 columns (256 bytes, up to 3 lines).
+        const int r = q * 32 + lane;
+        const int c0 = ti.n_blk * BN + h * (BN / 2);
+        if (r < min(BMC, ti.rows) && c0 < p.n_out) {
+          const int64_t e0 = (int64_t)(ti.row0 + r) * p.n_out + c0;
+          const int64_t e1 = e0 + min(BN / 2, p.n_out - c0) - 1;  // last element
+          const OutT* gsrc = static_cast<const OutT*>(p.in_gate);
+          const OutT* usrc = static_cast<const OutT*>(p.in_up);
+          for (int64_t e = e0; e <= e1 + 63; e += 64) {
+            const int64_t ee = e < e1 ? e : e1;
+            ptx::prefetch_l2(gsrc + ee);
+            ptx::prefetch_l2(usrc + ee);
+          }
+        }
+      }
       if (!wait_local(ptx::smem_u32(&s.tmem_full[buf]), acc_phase, abort_flag)) break;
       ptx::tc_fence_after();
       if constexpr (MODE == kModeGateUp) {

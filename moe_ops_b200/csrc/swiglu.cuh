@@ -17,6 +17,8 @@ namespace moe {
 template <typename T>
 __device__ __forceinline__ float rnd(float v) { return to_f32(from_f32<T>(v)); }
 
+// Logistic function in fp32 (expf and an IEEE division); every kernel that applies the
+// SwiGLU uses this one definition.
 __device__ __forceinline__ float sigmoid_f32(float x) { return 1.f / (1.f + expf(-x)); }
 
 template <typename T>
