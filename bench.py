@@ -46,9 +46,29 @@ CONFIGS = {
 }
 CFG = CONFIGS["cfg4"]
 METRIC = "moe_layer_fwd_bwd_grouped_gemm_tflops"
-# Pure DRAM write bandwidth of this part, measured (torch zero_ on 5.8 GB, profiles/
-# hbm_write_bandwidth.md); the copy figure in MEASURED_PEAKS.json mixes reads and writes.
-HBM_WRITE_GBS = 3912.0
+
+
+def _write_bandwidth(dev, nbytes=4 << 30, reps=5):
+    """DRAM write bandwidth (GB/s) of this GPU now: the library's 16-byte-store fill
+    (moe_write_probe) over a buffer far larger than L2, timed with CUDA events."""
+    from moe_ops_b200 import _lib
+
+    lib = _lib.load()
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def fill():
+        _lib.check(lib.moe_write_probe(buf.data_ptr(), nbytes, stream.cuda_stream), "moe_write_probe")
+
+    fill()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(reps):
+        fill()
+    ev1.record(stream)
+    ev1.synchronize()
+    del buf
+    return nbytes * reps / (ev0.elapsed_time(ev1) * 1e-3) / 1e9
 
 
 def _dist_env():
@@ -238,13 +258,14 @@ def run_ours(args):
     timing, _lib.gemm_timing = _lib.gemm_timing, None
     gemm_ms = sum(t[1].elapsed_time(t[2]) for t in timing)
     gemm_flops = sum(t[3] for t in timing)
-    # Per-launch roofline time: max(FLOPs / tensor peak, DRAM traffic / copy bandwidth,
-    # written bytes / pure-write bandwidth); writes are slower than reads on this part.
+    # Per-launch roofline time: max(FLOPs / tensor peak, DRAM bytes / copy bandwidth,
+    # written bytes / write bandwidth measured now on this GPU).
     peaks_, _ = _peaks()
+    write_gbs = _write_bandwidth(dev)
     t_roof = 0.0
     for t in timing:
         flop_s = t[3] / (peaks_.get("bf16_tflops_sustained", 1400.0) * 1e12)
-        mem_s = max((t[4] + t[5]) / (peaks_["hbm_gbs"] * 1e9), t[5] / (HBM_WRITE_GBS * 1e9))
+        mem_s = max((t[4] + t[5]) / (peaks_["hbm_gbs"] * 1e9), t[5] / (write_gbs * 1e9))
         t_roof += max(flop_s, mem_s)
 
     # ------------------------------------------------------------ end to end (host buffers)
@@ -329,8 +350,9 @@ def run_ours(args):
             "gemm_time_vs_roofline": round(t_roof * 1e3 / gemm_ms, 4) if gemm_ms else None,
             "roofline_note": "frac = achieved / tensor peak; gemm_time_vs_roofline = sum over "
                              "launches of max(FLOP/tensor peak, DRAM bytes/copy BW, written "
-                             f"bytes/{HBM_WRITE_GBS:.0f} GB/s write BW) / measured GEMM time",
+                             f"bytes/{write_gbs:.0f} GB/s write BW measured in this run) / measured GEMM time",
             "traffic": traffic.get("bytes_per_launch") if traffic else None,
+            "write_gbs": round(write_gbs, 1),
         },
         "e2e": {
             "value": round(e2e_value, 2), "unit": "TFLOP/s",
@@ -463,6 +485,11 @@ def run_case(args):
                     "ms": round(ms, 4), "tflops": round(tf, 1),
                     "frac_of_burst_peak": round(tf / peaks["bf16_tflops"], 4),
                     "peak_kind": kind})
+    elif args.case == "hbm-write":
+        # DRAM write bandwidth: 16-byte stores over 5.77 GB (one cfg4 weight gradient).
+        gbs = _write_bandwidth(dev, nbytes=5768732672, reps=max(args.steps, 1))
+        res.update({"GB/s": round(gbs, 1), "bytes": 5768732672,
+                    "frac_of_copy_peak": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": kind})
     elif args.case == "routing":
         T, d, E, K = 8192, 4096, 64, 2
         x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
@@ -501,7 +528,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg4",
                     help="layer workload: cfg4 (headline, default) or cfg5")
     ap.add_argument("--case", default="layer",
-                    help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing")
+                    help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing | hbm-write")
     ap.add_argument("--experts", type=int, default=None,
                     help="gmm-* cases: experts (cfg4 shapes, default 64); layer case: run a "
                          "slice of the config with this many experts (profiling)")

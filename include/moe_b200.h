@@ -54,6 +54,12 @@ int moe_read_device_error(int* code_out);
  * returns; the context stays usable. */
 int moe_selftest_bounded_wait(uint64_t timeout_ns, int32_t* result, void* stream);
 
+/* Measurement aid (no counterpart in the reference): writes zeros over `bytes` bytes at dst
+ * (16-byte aligned, bytes a multiple of 16) with 16-byte stores from 8 blocks per SM, the
+ * access size of the GEMM epilogues.  bench.py times it to measure this part's DRAM write
+ * bandwidth, a bound of the weight-gradient GEMM. */
+int moe_write_probe(void* dst, size_t bytes, void* stream);
+
 /* ---------------------------------------------------------------- top-k softmax
  * Replaces tg::fused_topk_softmax_fwd
  * (triton_gmm_ops/fused_topk_softmax_ops.py:121-138, kernel :17-70).

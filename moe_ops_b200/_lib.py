@@ -30,6 +30,7 @@ SIGNATURES = {
     "moe_last_error_string": (ctypes.c_char_p, []),
     "moe_read_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
     "moe_selftest_bounded_wait": (_c_int, [ctypes.c_uint64, _c_ptr, _c_ptr]),
+    "moe_write_probe": (_c_int, [_c_ptr, ctypes.c_size_t, _c_ptr]),
     "moe_topk_softmax_fwd": (_c_int, [_c_ptr, _c_int, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr]),
     "moe_topk_softmax_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr]),
     "moe_permute_workspace_bytes": (_c_size, [_c_i64, _c_i32, _c_i32]),

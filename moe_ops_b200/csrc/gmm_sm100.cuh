@@ -79,7 +79,10 @@ constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 16-bit columns (swiz
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
 #ifndef MOE_GMM_EPI_EXPERIMENT
-#define MOE_GMM_EPI_EXPERIMENT 0  // 1: no global stores, 2: no epilogue work (timing probes)
+// Timing probes (results are wrong when nonzero): 1 no masked global stores, 2 no epilogue
+// work, 3 no TMA stores, 4 no staging and no TMA stores, 5 no wait for the previous TMA
+// store's read of the staging buffer, 6 16-byte global stores in place of every TMA store.
+#define MOE_GMM_EPI_EXPERIMENT 0
 #endif
 
 template <int CG>
@@ -635,6 +638,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             ptx::tmem_ld_32x32b_x32(tbase + BN / 2 + col, vu);
             ptx::tmem_wait_ld();
             const int64_t off = (int64_t)(row_base + q * 32) * p.n_out + n0 + col;
+#pragma unroll
             for (int o = 0; o < 3; ++o) {
               if (o == 0) pack32_16b<OutT>(vg, wd);
               else if (o == 1) pack32_16b<OutT>(vu, wd);
@@ -735,7 +739,8 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // TMA stores clip at the output's edges, so they serve every wgrad tile and every
         // warp whose 32 rows all belong to the expert; the others store with masks so they
         // never touch the next expert's rows.  A warp with no valid row stores nothing.
-        const bool use_tma = MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows;
+        const bool use_tma = MOE_GMM_EPI_EXPERIMENT != 6 &&
+                             (MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows);
   #if MOE_GMM_EPI_EXPERIMENT == 2
         const int nchunks = 0;
   #else
@@ -764,18 +769,24 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             for (int i = 0; i < 16; ++i) w[i] = 0u;
           }
           // The previous TMA store from this buffer must have finished reading it.
+  #if MOE_GMM_EPI_EXPERIMENT != 5
           if (lane == 0) ptx::bulk_wait_group_read<0>();
+  #endif
           __syncwarp();
+  #if MOE_GMM_EPI_EXPERIMENT != 4
   #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int phys = i ^ ((wr_row >> 1) & 3);
             *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
                 make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
           }
+  #else
+          if (w[0] == 0x7fc00001u && w[15] == 0x7fc00001u) *reinterpret_cast<uint4*>(cbuf) = make_uint4(w[1], w[2], w[3], w[4]);
+  #endif
           if (use_tma) {
             ptx::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) {
+            if (lane == 0 && MOE_GMM_EPI_EXPERIMENT != 3 && MOE_GMM_EPI_EXPERIMENT != 4) {
               const int cx = n0 + col_lo + c * 32;
               if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
               else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
@@ -792,7 +803,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             const int phys = rd_chunk ^ ((rr >> 1) & 3);
             const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
             const int row = rq * 32 + rr;
-  #if MOE_GMM_EPI_EXPERIMENT == 0
+  #if MOE_GMM_EPI_EXPERIMENT == 0 || MOE_GMM_EPI_EXPERIMENT == 6
             if (row < valid_rows && col < valid_cols)
               *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;
   #else

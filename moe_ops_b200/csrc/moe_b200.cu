@@ -371,6 +371,13 @@ static PermuteWorkspace permute_ws(int64_t T, int K, int E) {
   return w;
 }
 
+// Zero fill with 16-byte stores (the write-bandwidth probe).
+__global__ void __launch_bounds__(256) write_probe_kernel(uint4* __restrict__ p, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    p[i] = make_uint4(0, 0, 0, 0);
+}
+
 // Grid of the grid-stride elementwise kernels: up to 8 blocks of 256 threads per SM.
 static unsigned elementwise_grid(int64_t n, int per_thread) {
   const int64_t blocks = (n / per_thread + 255) / 256;
@@ -830,6 +837,16 @@ int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, in
   return moe_permute(input, dtype, indices, num_tokens, topk, num_cols, E, num_out, permuted,
                      row_id_map, offsets, g_permute_scratch_ptr[dev],
                      kNoAllocScratchInts * sizeof(int32_t), stream);
+}
+
+int moe_write_probe(void* dst, size_t bytes, void* stream) {
+  MOE_REQUIRE(aligned16(dst) && bytes % 16 == 0, "write_probe: dst and bytes must be 16-byte multiples");
+  if (bytes == 0) return MOE_OK;
+  const int64_t n = (int64_t)(bytes / 16);
+  write_probe_kernel<<<elementwise_grid(n * 16, 16), 256, 0, (cudaStream_t)stream>>>(
+      static_cast<uint4*>(dst), n);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
 }
 
 int moe_selftest_bounded_wait(uint64_t timeout_ns, int32_t* result, void* stream) {
