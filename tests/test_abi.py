@@ -91,3 +91,60 @@ def test_fake_impls_give_reference_shapes():
         assert p.shape == (100, 64) and r.shape == (100,) and o.shape == (9,)
         w, i = torch.ops.moeb200.fused_topk_softmax_fwd(torch.empty(50, 8), 2)
         assert w.shape == (50, 2) and i.dtype == torch.int32
+
+
+def test_every_custom_op_has_a_fake_impl():
+    """Each torch.ops.moeb200 op runs under FakeTensorMode (what torch.compile traces with)
+    and returns the shapes and dtypes the real op returns.  The list below must name every
+    op the package registers."""
+    import glob
+    import re
+
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import moe_ops_b200  # noqa: F401  (registers the ops)
+    from moe_ops_b200 import gate_up_ops, swiglu_ops  # noqa: F401
+
+    bf = torch.bfloat16
+    ops = torch.ops.moeb200
+    T, K, E, d, H = 50, 2, 8, 64, 96
+    with FakeTensorMode():
+        x = torch.empty(T, d, dtype=bf)
+        A = torch.empty(T * K, d, dtype=bf)
+        off = torch.empty(E + 1, dtype=torch.int32)
+        Wgu = torch.empty(E, H, d, dtype=bf)
+        Wd = torch.empty(E, d, H, dtype=bf)
+        idx = torch.empty(T, K, dtype=torch.int32)
+        rid = torch.empty(T * K, dtype=torch.int32)
+        prob = torch.empty(T, K)
+        gate = torch.empty(T * K, H, dtype=bf)
+        checks = {
+            "gmm_fwd_raw": (ops.gmm_fwd_raw(A, Wgu, off, True), [((T * K, H), bf)]),
+            "gmm_dgrad_raw": (ops.gmm_dgrad_raw(gate, Wgu, off, True), [((T * K, d), bf)]),
+            "gmm_bwd_B_raw": (ops.gmm_bwd_B_raw(A, Wgu, off, gate, True), [((E, H, d), bf)]),
+            "gmm_gate_up_fwd_raw": (ops.gmm_gate_up_fwd_raw(A, Wgu, Wgu, off, True),
+                                    [((T * K, H), bf)] * 3),
+            "gmm_dgrad_swiglu_bwd_raw": (
+                ops.gmm_dgrad_swiglu_bwd_raw(A, Wd, gate, gate, off, True), [((T * K, H), bf)] * 2),
+            "permute_countsort": (ops.permute_countsort(x, idx, 0, E),
+                                  [((T * K, d), bf), ((T * K,), torch.int32), ((E + 1,), torch.int32)]),
+            "scatter_rows": (ops.scatter_rows(x, rid, T * K, K), [((T * K, d), bf)]),
+            "unpermute_forward": (ops.unpermute_forward(A, rid, prob, T, K), [((T, d), bf)]),
+            "unpermute_backward": (ops.unpermute_backward(x, A, rid, prob, T, K),
+                                   [((T * K, d), bf), ((T, K), torch.float32)]),
+            "fused_topk_softmax_fwd": (ops.fused_topk_softmax_fwd(torch.empty(T, E), K),
+                                       [((T, K), torch.float32), ((T, K), torch.int32)]),
+            "fused_topk_softmax_bwd": (
+                ops.fused_topk_softmax_bwd(prob, prob, idx, T, E, K), [((T, E), torch.float32)]),
+            "swiglu_fwd": (ops.swiglu_fwd(gate, gate), [((T * K, H), bf)]),
+            "swiglu_bwd": (ops.swiglu_bwd(gate, gate, gate), [((T * K, H), bf)] * 2),
+        }
+    for name, (out, want) in checks.items():
+        outs = out if isinstance(out, (tuple, list)) else (out,)
+        got = [(tuple(o.shape), o.dtype) for o in outs]
+        assert got == want, f"{name}: fake gives {got}, expected {want}"
+    registered = set()
+    for path in glob.glob(os.path.join(REPO, "moe_ops_b200", "*.py")):
+        registered |= set(re.findall(r'custom_op\(f"\{_NS\}::([A-Za-z0-9_]+)"', open(path).read()))
+    assert registered == set(checks), (f"untested: {sorted(registered - set(checks))}, "
+                                       f"not registered: {sorted(set(checks) - registered)}")
+
