@@ -190,6 +190,60 @@ int moe_gmm_dgrad_swiglu_bwd(const void* grad_C, const void* B, const void* gate
                              int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
                              int32_t num_experts, int trans_b, int dtype, void* stream);
 
+/* ---------------------------------------------------------------- expert parallelism over peer memory
+ * No counterpart in the reference, which has no multi-GPU path: the dispatch and combine of
+ * an expert-parallel layer, moving rows between the GPUs' buffers over NVLink in place of
+ * an all-to-all.  Rank r owns experts [r*El, (r+1)*El).  `bases` / `in_bases` /
+ * `act_bases` / `flags` are DEVICE arrays of `world` pointers: entry r is rank r's buffer as
+ * mapped in this process (this rank's own allocation, or a peer's opened with
+ * moe_ipc_open).  Every row a kernel touches is checked against the receive capacity first;
+ * a bad slot is skipped and raises device error 3. */
+
+/* cudaMalloc of `bytes` plus its CUDA IPC handle (64 bytes written to `handle`), for a
+ * buffer the peers map with moe_ipc_open. */
+int moe_ipc_malloc(size_t bytes, void** ptr, void* handle);
+/* Maps a peer's buffer (its 64-byte IPC handle) into this process. */
+int moe_ipc_open(const void* handle, void** ptr);
+int moe_ipc_close(void* ptr);
+int moe_ipc_free(void* ptr);
+
+/* Destination of every slot: slot j = k*T + t with expert e = indices[t*K+k] goes to rank
+ * e / experts_per_rank at row row_id_map[j] + delta[e] (row_id_map from moe_permute over
+ * the global experts; delta[e] places this rank's rows of expert e in the owner's receive
+ * buffer).  ranks[j] = -1 (and device error 3) when e or the row is out of range. */
+int moe_ep_slot_map(const int32_t* indices, const int32_t* row_id_map, const int32_t* delta,
+                    int64_t num_tokens, int32_t topk, int32_t num_experts,
+                    int32_t experts_per_rank, int32_t world, int64_t capacity, int32_t* ranks,
+                    int32_t* rows, void* stream);
+/* Dispatch: input row t to bases[ranks[j]] row rows[j] for each of its K slots (the
+ * permute copy with peer destinations). */
+int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int32_t* ranks,
+                    const int32_t* rows, int64_t num_tokens, int32_t topk, int64_t num_cols,
+                    void* stream);
+/* Combine: out[t] = sum_k prob[t,k] * row(slot k of t) read from bases[ranks[j]], with the
+ * rounding of moe_unpermute_fwd; prob NULL means 1 (the dispatch's backward). */
+int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, const int32_t* rows,
+                   const void* prob, int prob_dtype, int64_t num_tokens, int32_t topk,
+                   int64_t num_cols, void* out, void* stream);
+/* Combine backward (moe_unpermute_bwd over peer rows): act row of slot j (in act_bases) =
+ * grad_out[t] * prob[t,k]; prob_grad[t,k] = <grad_out[t], row of slot j in in_bases>. */
+int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* const* act_bases,
+                       int dtype, const int32_t* ranks, const int32_t* rows, const void* prob,
+                       int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols,
+                       void* prob_grad, void* stream);
+/* dst[r] += src[r] (fp32 sum rounded to dtype) for rows r < min(*n_rows, max_rows) of two
+ * [max_rows, num_cols] buffers; n_rows is a device int32 (e.g. the last grouped-GEMM
+ * offset), so worst-case-sized buffers cost only their live rows. */
+int moe_add_rows(void* dst, const void* src, const int32_t* n_rows, int64_t max_rows,
+                 int64_t num_cols, int dtype, void* stream);
+/* Cross-GPU barrier on `world` int64 flag arrays of `world` slots each (one per rank, in
+ * IPC memory): writes `epoch` to slot `rank` of every rank's array (after a system-scope
+ * fence), then waits until every slot of this rank's array reaches `epoch`.  Gives up after
+ * timeout_ns: *status (device int32, may be NULL) = 0 and device error 4; else 1.  Epochs
+ * must increase by one per barrier.  The ranks must run on different GPUs. */
+int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t epoch,
+                   uint64_t timeout_ns, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

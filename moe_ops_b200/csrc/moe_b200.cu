@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "ep_peer.cuh"
 #include "gmm_simt.cuh"
 #include "gmm_sm100.cuh"
 #include "permute.cuh"
@@ -498,12 +499,15 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   const bool vec = (num_cols * es) % 16 == 0 && aligned16(input) && aligned16(permuted);
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
 #define MOE_COPY(TT)                                                                                 \
-  if (vec)                                                                                          \
-    permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>(                                   \
-        (const TT*)input, row_id_map, (TT*)permuted, num_tokens, topk, num_cols);                  \
-  else                                                                                              \
-    permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>(                                  \
-        (const TT*)input, row_id_map, (TT*)permuted, num_tokens, topk, num_cols);
+  {                                                                                                 \
+    const LocalRows<TT> rows{(TT*)permuted, row_id_map, num_tokens, num_cols};                      \
+    if (vec)                                                                                        \
+      permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,          \
+                                                                    num_tokens, topk, num_cols);   \
+    else                                                                                            \
+      permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,         \
+                                                                     num_tokens, topk, num_cols);  \
+  }
   switch (dtype) {
     case MOE_F32: MOE_COPY(float) break;
     case MOE_F16: MOE_COPY(__half) break;
@@ -549,12 +553,15 @@ int moe_scatter_rows(const void* input, int dtype, const int32_t* row_id_map, in
   const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0 && aligned16(input) && aligned16(out);
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
 #define MOE_SC(TT)                                                                                   \
-  if (vec)                                                                                          \
-    permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>(                                   \
-        (const TT*)input, row_id_map, (TT*)out, num_tokens, topk, num_cols);                       \
-  else                                                                                              \
-    permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>(                                  \
-        (const TT*)input, row_id_map, (TT*)out, num_tokens, topk, num_cols);
+  {                                                                                                 \
+    const LocalRows<TT> rows{(TT*)out, row_id_map, num_tokens, num_cols};                           \
+    if (vec)                                                                                        \
+      permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,          \
+                                                                    num_tokens, topk, num_cols);   \
+    else                                                                                            \
+      permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,         \
+                                                                     num_tokens, topk, num_cols);  \
+  }
   switch (dtype) {
     case MOE_F32: MOE_SC(float) break;
     case MOE_F16: MOE_SC(__half) break;
@@ -578,12 +585,15 @@ int moe_unpermute_fwd(const void* input, int dtype, const int32_t* row_id_map, c
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
   const int pd = prob == nullptr ? MOE_F32 : prob_dtype;
 #define MOE_UNP(TT, PP)                                                                              \
-  if (vec)                                                                                          \
-    unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                              \
-        (const TT*)input, row_id_map, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);      \
-  else                                                                                              \
-    unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                             \
-        (const TT*)input, row_id_map, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);
+  {                                                                                                 \
+    const LocalRows<const TT> rows{(const TT*)input, row_id_map, num_tokens, num_cols};             \
+    if (vec)                                                                                        \
+      unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                            \
+          rows, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                             \
+    else                                                                                            \
+      unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                           \
+          rows, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                             \
+  }
 #define MOE_UNP_P(TT)                                                                                \
   switch (pd) {                                                                                     \
     case MOE_F32: MOE_UNP(TT, float) break;                                                         \
@@ -615,14 +625,18 @@ int moe_unpermute_bwd(const void* grad_out, const void* input_fwd, int dtype,
                    aligned16(act_grad);
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
 #define MOE_UB(TT, PP, KM)                                                                           \
-  if (vec)                                                                                          \
-    unpermute_bwd_kernel<TT, PP, KM, true><<<grid, kRowWarps * 32, 0, s>>>(                          \
-        (const TT*)grad_out, (const TT*)input_fwd, row_id_map, (const PP*)prob, (TT*)act_grad,     \
-        (PP*)prob_grad, num_tokens, topk, num_cols);                                               \
-  else                                                                                              \
-    unpermute_bwd_kernel<TT, PP, KM, false><<<grid, kRowWarps * 32, 0, s>>>(                         \
-        (const TT*)grad_out, (const TT*)input_fwd, row_id_map, (const PP*)prob, (TT*)act_grad,     \
-        (PP*)prob_grad, num_tokens, topk, num_cols);
+  {                                                                                                 \
+    const LocalRows<const TT> in_rows{(const TT*)input_fwd, row_id_map, num_tokens, num_cols};      \
+    const LocalRows<TT> act_rows{(TT*)act_grad, row_id_map, num_tokens, num_cols};                  \
+    if (vec)                                                                                        \
+      unpermute_bwd_kernel<TT, PP, KM, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
+          (const TT*)grad_out, in_rows, act_rows, (const PP*)prob, (PP*)prob_grad, num_tokens,      \
+          topk, num_cols);                                                                          \
+    else                                                                                            \
+      unpermute_bwd_kernel<TT, PP, KM, false><<<grid, kRowWarps * 32, 0, s>>>(                       \
+          (const TT*)grad_out, in_rows, act_rows, (const PP*)prob, (PP*)prob_grad, num_tokens,      \
+          topk, num_cols);                                                                          \
+  }
 #define MOE_UB_K(TT, PP)                                                                             \
   if (topk <= 2) { MOE_UB(TT, PP, 2) }                                                              \
   else if (topk <= 4) { MOE_UB(TT, PP, 4) }                                                         \
@@ -837,6 +851,204 @@ int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, in
   return moe_permute(input, dtype, indices, num_tokens, topk, num_cols, E, num_out, permuted,
                      row_id_map, offsets, g_permute_scratch_ptr[dev],
                      kNoAllocScratchInts * sizeof(int32_t), stream);
+}
+
+// ---------------------------------------------------------------- expert parallelism over peer memory
+int moe_ipc_malloc(size_t bytes, void** ptr, void* handle) {
+  MOE_REQUIRE(ptr != nullptr && handle != nullptr && bytes > 0, "ipc_malloc: bad arguments");
+  MOE_CUDA_CHECK(cudaMalloc(ptr, bytes));
+  const cudaError_t e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return set_error(MOE_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  }
+  return MOE_OK;
+}
+
+int moe_ipc_open(const void* handle, void** ptr) {
+  MOE_REQUIRE(ptr != nullptr && handle != nullptr, "ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  MOE_CUDA_CHECK(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MOE_OK;
+}
+
+int moe_ipc_close(void* ptr) {
+  MOE_CUDA_CHECK(cudaIpcCloseMemHandle(ptr));
+  return MOE_OK;
+}
+
+int moe_ipc_free(void* ptr) {
+  MOE_CUDA_CHECK(cudaFree(ptr));
+  return MOE_OK;
+}
+
+int moe_ep_slot_map(const int32_t* indices, const int32_t* row_id_map, const int32_t* delta,
+                    int64_t num_tokens, int32_t topk, int32_t E, int32_t experts_per_rank,
+                    int32_t world, int64_t capacity, int32_t* ranks, int32_t* rows, void* stream) {
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && E > 0 && experts_per_rank > 0 &&
+                  world > 0 && E == experts_per_rank * world && capacity >= 0 &&
+                  capacity < (1ll << 31),
+              "ep_slot_map: bad sizes T=%lld K=%d E=%d El=%d W=%d", (long long)num_tokens, topk,
+              E, experts_per_rank, world);
+  const int64_t n = num_tokens * topk;
+  if (n == 0) return MOE_OK;
+  const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms(current_device()) * 8);
+  ep_slot_map_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(indices, row_id_map, delta, num_tokens,
+                                                             topk, E, experts_per_rank, world,
+                                                             capacity, ranks, rows);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int32_t* ranks,
+                    const int32_t* rows, int64_t num_tokens, int32_t topk, int64_t num_cols,
+                    void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "ep_dispatch: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_dispatch: bad sizes");
+  MOE_REQUIRE(aligned16(input), "ep_dispatch: input must be 16-byte aligned");
+  if (num_tokens == 0 || num_cols == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  // Receive buffers are 256-byte aligned allocations; rows are 16-byte multiples or not,
+  // the same for every rank.
+  const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0;
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+#define MOE_EPD(TT)                                                                                  \
+  {                                                                                                 \
+    const PeerRows<TT> r{(TT* const*)bases, ranks, rows, num_tokens, num_cols};                      \
+    if (vec)                                                                                        \
+      permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, r,             \
+                                                                    num_tokens, topk, num_cols);   \
+    else                                                                                            \
+      permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, r,            \
+                                                                     num_tokens, topk, num_cols);  \
+  }
+  switch (dtype) {
+    case MOE_F32: MOE_EPD(float) break;
+    case MOE_F16: MOE_EPD(__half) break;
+    default: MOE_EPD(__nv_bfloat16) break;
+  }
+#undef MOE_EPD
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, const int32_t* rows,
+                   const void* prob, int prob_dtype, int64_t num_tokens, int32_t topk,
+                   int64_t num_cols, void* out, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype) && (prob == nullptr || dtype_ok(prob_dtype)),
+              "ep_combine: bad dtype %d / prob dtype %d", dtype, prob_dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_combine: bad sizes");
+  MOE_REQUIRE(aligned16(out), "ep_combine: out must be 16-byte aligned");
+  if (num_tokens == 0 || num_cols == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0;
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+  const int pd = prob == nullptr ? MOE_F32 : prob_dtype;
+#define MOE_EPC(TT, PP)                                                                              \
+  {                                                                                                 \
+    const PeerRows<const TT> r{(const TT* const*)bases, ranks, rows, num_tokens, num_cols};          \
+    if (vec)                                                                                        \
+      unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                            \
+          r, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+    else                                                                                            \
+      unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                           \
+          r, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+  }
+#define MOE_EPC_P(TT)                                                                                \
+  switch (pd) {                                                                                     \
+    case MOE_F32: MOE_EPC(TT, float) break;                                                         \
+    case MOE_F16: MOE_EPC(TT, __half) break;                                                        \
+    default: MOE_EPC(TT, __nv_bfloat16) break;                                                      \
+  }
+  switch (dtype) {
+    case MOE_F32: MOE_EPC_P(float) break;
+    case MOE_F16: MOE_EPC_P(__half) break;
+    default: MOE_EPC_P(__nv_bfloat16) break;
+  }
+#undef MOE_EPC_P
+#undef MOE_EPC
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* const* act_bases,
+                       int dtype, const int32_t* ranks, const int32_t* rows, const void* prob,
+                       int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols,
+                       void* prob_grad, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype) && dtype_ok(prob_dtype), "ep_combine_bwd: bad dtype");
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_combine_bwd: bad sizes");
+  MOE_REQUIRE(prob != nullptr && prob_grad != nullptr, "ep_combine_bwd: prob / prob_grad is NULL");
+  MOE_REQUIRE(aligned16(grad_out), "ep_combine_bwd: grad_out must be 16-byte aligned");
+  if (num_tokens == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0;
+  const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
+#define MOE_EPB(TT, PP, KM)                                                                          \
+  {                                                                                                 \
+    const PeerRows<const TT> ir{(const TT* const*)in_bases, ranks, rows, num_tokens, num_cols};     \
+    const PeerRows<TT> ar{(TT* const*)act_bases, ranks, rows, num_tokens, num_cols};                \
+    if (vec)                                                                                        \
+      unpermute_bwd_kernel<TT, PP, KM, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
+          (const TT*)grad_out, ir, ar, (const PP*)prob, (PP*)prob_grad, num_tokens, topk, num_cols);\
+    else                                                                                            \
+      unpermute_bwd_kernel<TT, PP, KM, false><<<grid, kRowWarps * 32, 0, s>>>(                       \
+          (const TT*)grad_out, ir, ar, (const PP*)prob, (PP*)prob_grad, num_tokens, topk, num_cols);\
+  }
+#define MOE_EPB_K(TT, PP)                                                                            \
+  if (topk <= 2) { MOE_EPB(TT, PP, 2) }                                                             \
+  else if (topk <= 4) { MOE_EPB(TT, PP, 4) }                                                        \
+  else if (topk <= 8) { MOE_EPB(TT, PP, 8) }                                                        \
+  else if (topk <= 16) { MOE_EPB(TT, PP, 16) }                                                      \
+  else { MOE_EPB(TT, PP, 32) }
+#define MOE_EPB_P(TT)                                                                                \
+  switch (prob_dtype) {                                                                             \
+    case MOE_F32: MOE_EPB_K(TT, float) break;                                                       \
+    case MOE_F16: MOE_EPB_K(TT, __half) break;                                                      \
+    default: MOE_EPB_K(TT, __nv_bfloat16) break;                                                    \
+  }
+  switch (dtype) {
+    case MOE_F32: MOE_EPB_P(float) break;
+    case MOE_F16: MOE_EPB_P(__half) break;
+    default: MOE_EPB_P(__nv_bfloat16) break;
+  }
+#undef MOE_EPB_P
+#undef MOE_EPB_K
+#undef MOE_EPB
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_add_rows(void* dst, const void* src, const int32_t* n_rows, int64_t max_rows,
+                 int64_t num_cols, int dtype, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype) && max_rows >= 0 && num_cols >= 0 && n_rows != nullptr,
+              "add_rows: bad arguments");
+  if (max_rows == 0 || num_cols == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool vec = (num_cols * dtype_size(dtype)) % 16 == 0 && aligned16(dst) && aligned16(src);
+  const unsigned grid = elementwise_grid(max_rows * num_cols, vec ? 16 / dtype_size(dtype) : 1);
+#define MOE_ADD(TT)                                                                                  \
+  if (vec) add_rows_kernel<TT, true><<<grid, 256, 0, s>>>((TT*)dst, (const TT*)src, n_rows, max_rows, num_cols); \
+  else add_rows_kernel<TT, false><<<grid, 256, 0, s>>>((TT*)dst, (const TT*)src, n_rows, max_rows, num_cols);
+  switch (dtype) {
+    case MOE_F32: MOE_ADD(float) break;
+    case MOE_F16: MOE_ADD(__half) break;
+    default: MOE_ADD(__nv_bfloat16) break;
+  }
+#undef MOE_ADD
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t epoch,
+                   uint64_t timeout_ns, int32_t* status, void* stream) {
+  MOE_REQUIRE(flags != nullptr && world > 0 && world <= 32 && rank >= 0 && rank < world && epoch > 0,
+              "ep_barrier: bad arguments rank=%d world=%d", rank, world);
+  MOE_REQUIRE(timeout_ns <= 10000000000ull, "ep_barrier: timeout above 10 s");
+  ep_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, rank, world, epoch, timeout_ns, status);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
 }
 
 int moe_write_probe(void* dst, size_t bytes, void* stream) {

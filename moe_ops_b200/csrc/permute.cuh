@@ -171,17 +171,57 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
 
 constexpr int kRowWarps = 8;  // warps (tokens) per block for the row kernels
 
+// Where the K rows of token t live.  The row kernels below read a slot's (rank, row) in lane
+// k, broadcast it with shuffles and turn it into a pointer with at().
+//   LocalRows: one buffer, rows from row_id_map (k-major [K*T], -1 = no row).
+//   PeerRows:  rows spread over the ranks' buffers (expert parallelism over peer memory):
+//              slot j = k*T + t lives in bases[ranks[j]] at row rows[j]; ranks[j] < 0 = none.
+template <typename T>
+struct LocalRows {
+  static constexpr bool kPeer = false;
+  T* base;
+  const int32_t* map;
+  int64_t num_tokens, num_cols;
+  __device__ __forceinline__ int32_t row(int k, int64_t t) const {
+    return map[(int64_t)k * num_tokens + t];
+  }
+  __device__ __forceinline__ int32_t rank(int, int64_t) const { return 0; }
+  __device__ __forceinline__ T* at(int32_t, int32_t r) const { return base + (int64_t)r * num_cols; }
+};
+
+template <typename T>
+struct PeerRows {
+  static constexpr bool kPeer = true;
+  T* const* bases;
+  const int32_t* ranks;
+  const int32_t* rows;
+  int64_t num_tokens, num_cols;
+  __device__ __forceinline__ int32_t row(int k, int64_t t) const {
+    const int64_t j = (int64_t)k * num_tokens + t;
+    return ranks[j] < 0 ? -1 : rows[j];
+  }
+  __device__ __forceinline__ int32_t rank(int k, int64_t t) const {
+    return ranks[(int64_t)k * num_tokens + t];
+  }
+  __device__ __forceinline__ T* at(int32_t rk, int32_t r) const {
+    return bases[rk] + (int64_t)r * num_cols;
+  }
+};
+
 // ---------------------------------------------------------------- 4. copy (token-major)
 // VEC: rows are 16-byte multiples and 16-byte aligned (uint4 path), else element path.
-template <typename T, bool VEC>
+template <typename T, bool VEC, class Rows>
 __global__ void __launch_bounds__(kRowWarps * 32)
-permute_copy_kernel(const T* __restrict__ input, const int32_t* __restrict__ row_id_map,
-                    T* __restrict__ permuted, int64_t num_tokens, int K, int64_t num_cols) {
+permute_copy_kernel(const T* __restrict__ input, Rows dst_rows, int64_t num_tokens, int K,
+                    int64_t num_cols) {
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (t >= num_tokens) return;
-  int32_t dst_lane = -1;
-  if (lane < K) dst_lane = row_id_map[(int64_t)lane * num_tokens + t];
+  int32_t dst_lane = -1, rank_lane = 0;
+  if (lane < K) {
+    dst_lane = dst_rows.row(lane, t);
+    if constexpr (Rows::kPeer) rank_lane = dst_rows.rank(lane, t);
+  }
   const T* src = input + t * num_cols;
   if constexpr (VEC) {
     const int64_t nv = num_cols / Vec16<T>::N;
@@ -196,8 +236,9 @@ permute_copy_kernel(const T* __restrict__ input, const int32_t* __restrict__ row
       }
       for (int k = 0; k < K; ++k) {
         const int32_t d = __shfl_sync(0xffffffffu, dst_lane, k);
+        const int32_t rk = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
         if (d < 0) continue;
-        uint4* d4 = reinterpret_cast<uint4*>(permuted + (int64_t)d * num_cols);
+        uint4* d4 = reinterpret_cast<uint4*>(dst_rows.at(rk, d));
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int64_t c = c0 + u * 32 + lane;
@@ -213,7 +254,8 @@ permute_copy_kernel(const T* __restrict__ input, const int32_t* __restrict__ row
       const T v = in ? src[c] : T();
       for (int k = 0; k < K; ++k) {
         const int32_t d = __shfl_sync(0xffffffffu, dst_lane, k);
-        if (in && d >= 0) permuted[(int64_t)d * num_cols + c] = v;
+        const int32_t rk = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
+        if (in && d >= 0) dst_rows.at(rk, d)[c] = v;
       }
     }
   }
@@ -224,18 +266,18 @@ permute_copy_kernel(const T* __restrict__ input, const int32_t* __restrict__ row
 // Accumulation: acc = 0; acc = rn(acc + rn(v * p)) for k = 0..K-1 (no FMA contraction),
 // which is the rounding sequence of the reference's PyTorch oracle
 // (tests/test_unpermute.py:25-35).  A slot with row -1 contributes nothing.
-template <typename T, typename P, bool VEC>
+template <typename T, typename P, bool VEC, class Rows>
 __global__ void __launch_bounds__(kRowWarps * 32)
-unpermute_fwd_kernel(const T* __restrict__ input, const int32_t* __restrict__ row_id_map,
-                     const P* __restrict__ prob, T* __restrict__ out, int64_t num_tokens, int K,
-                     int64_t num_cols) {
+unpermute_fwd_kernel(Rows src_rows, const P* __restrict__ prob, T* __restrict__ out,
+                     int64_t num_tokens, int K, int64_t num_cols) {
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (t >= num_tokens) return;
-  int32_t src_lane = -1;
+  int32_t src_lane = -1, rank_lane = 0;
   float p_lane = 1.f;
   if (lane < K) {
-    src_lane = row_id_map[(int64_t)lane * num_tokens + t];
+    src_lane = src_rows.row(lane, t);
+    if constexpr (Rows::kPeer) rank_lane = src_rows.rank(lane, t);
     if (prob != nullptr) p_lane = to_f32(prob[t * K + lane]);
   }
   T* dst = out + t * num_cols;
@@ -251,9 +293,10 @@ unpermute_fwd_kernel(const T* __restrict__ input, const int32_t* __restrict__ ro
         for (int i = 0; i < NV; ++i) acc[u][i] = 0.f;
       for (int k = 0; k < K; ++k) {
         const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
+        const int32_t rk = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
         const float p = __shfl_sync(0xffffffffu, p_lane, k);
         if (s < 0) continue;
-        const uint4* s4 = reinterpret_cast<const uint4*>(input + (int64_t)s * num_cols);
+        const uint4* s4 = reinterpret_cast<const uint4*>(src_rows.at(rk, s));
         uint4 raw[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -282,9 +325,10 @@ unpermute_fwd_kernel(const T* __restrict__ input, const int32_t* __restrict__ ro
       float acc = 0.f;
       for (int k = 0; k < K; ++k) {
         const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
+        const int32_t rk = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
         const float p = __shfl_sync(0xffffffffu, p_lane, k);
         if (s < 0 || !in) continue;
-        acc = __fadd_rn(acc, __fmul_rn(to_f32(input[(int64_t)s * num_cols + c]), p));
+        acc = __fadd_rn(acc, __fmul_rn(to_f32(src_rows.at(rk, s)[c]), p));
       }
       if (in) dst[c] = from_f32<T>(acc);
     }
@@ -296,19 +340,22 @@ unpermute_fwd_kernel(const T* __restrict__ input, const int32_t* __restrict__ ro
 // i = row_id_map[k*T+t].  grad_out[t] is read once per column block and reused for all K
 // slots.  KMAX is the compile-time bound on K (the per-slot dot products live in
 // registers).
-template <typename T, typename P, int KMAX, bool VEC>
+// in_rows and act_rows share one slot map (the same rank and row for each slot); they differ
+// in the buffers they point into.
+template <typename T, typename P, int KMAX, bool VEC, class RowsIn, class RowsOut>
 __global__ void __launch_bounds__(kRowWarps * 32)
-unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input,
-                     const int32_t* __restrict__ row_id_map, const P* __restrict__ prob,
-                     T* __restrict__ act_grad, P* __restrict__ prob_grad, int64_t num_tokens,
+unpermute_bwd_kernel(const T* __restrict__ grad_out, RowsIn in_rows, RowsOut act_rows,
+                     const P* __restrict__ prob, P* __restrict__ prob_grad, int64_t num_tokens,
                      int K, int64_t num_cols) {
+  static_assert(RowsIn::kPeer == RowsOut::kPeer, "one slot map for both row sets");
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (t >= num_tokens) return;
-  int32_t src_lane = -1;
+  int32_t src_lane = -1, rank_lane = 0;
   float p_lane = 0.f;
   if (lane < K) {
-    src_lane = row_id_map[(int64_t)lane * num_tokens + t];
+    src_lane = in_rows.row(lane, t);
+    if constexpr (RowsIn::kPeer) rank_lane = in_rows.rank(lane, t);
     p_lane = to_f32(prob[t * K + lane]);
   }
   float dot[KMAX];
@@ -317,10 +364,12 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
   const T* g_row = grad_out + t * num_cols;
   // Slot rows and probabilities, broadcast once (K <= KMAX <= 32).
   int32_t src_k[KMAX];
+  int32_t rank_k[RowsIn::kPeer ? KMAX : 1];
   float p_k[KMAX];
 #pragma unroll
   for (int k = 0; k < KMAX; ++k) {
     src_k[k] = __shfl_sync(0xffffffffu, src_lane, k);
+    if constexpr (RowsIn::kPeer) rank_k[k] = __shfl_sync(0xffffffffu, rank_lane, k);
     p_k[k] = __shfl_sync(0xffffffffu, p_lane, k);
   }
   if constexpr (VEC) {
@@ -341,7 +390,9 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
         const int32_t s = src_k[k];
         const float p = p_k[k];
         if (s < 0) continue;
-        const uint4* in4 = reinterpret_cast<const uint4*>(input + (int64_t)s * num_cols);
+        const int32_t rk = RowsIn::kPeer ? rank_k[RowsIn::kPeer ? k : 0] : 0;
+        const uint4* in4 = reinterpret_cast<const uint4*>(in_rows.at(rk, s));
+        uint4* ag4 = reinterpret_cast<uint4*>(act_rows.at(rk, s));
         uint4 vraw[U];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -360,7 +411,7 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
             dot[k] = fmaf(g[i], v[i], dot[k]);
             ag[i] = __fmul_rn(g[i], p);
           }
-          reinterpret_cast<uint4*>(act_grad + (int64_t)s * num_cols)[c] = pack16<T>(ag);
+          ag4[c] = pack16<T>(ag);
         }
       }
     }
@@ -373,9 +424,10 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, const T* __restrict__ input
         const int32_t s = src_k[k];
         const float p = p_k[k];
         if (s < 0) continue;
-        const float v = to_f32(input[(int64_t)s * num_cols + c]);
+        const int32_t rk = RowsIn::kPeer ? rank_k[RowsIn::kPeer ? k : 0] : 0;
+        const float v = to_f32(in_rows.at(rk, s)[c]);
         dot[k] = fmaf(g, v, dot[k]);
-        act_grad[(int64_t)s * num_cols + c] = from_f32<T>(__fmul_rn(g, p));
+        act_rows.at(rk, s)[c] = from_f32<T>(__fmul_rn(g, p));
       }
     }
   }

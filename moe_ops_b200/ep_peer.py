@@ -1,0 +1,261 @@
+"""Expert parallelism with dispatch and combine over NVLink peer memory.
+
+The NCCL path in ``ep.py`` permutes locally, runs a row all-to-all, then regroups. Here
+the GPUs write and read each other's buffers directly, and the routing bookkeeping never
+reaches the host. Each rank's receive buffer is already the grouped GEMM's layout:
+expert-major, then source-rank-major.
+
+Per layer step (rank r of W, El = E / W local experts):
+
+    forward   permute index pass (no copy) -> counts all-gather (NCCL, device only)
+              -> delta / offsets (tiny tensor ops) -> slot map
+              -> B1 -> dispatch: rows straight into the owners' receive buffers
+              -> B2 -> gate/up + SwiGLU, down GEMMs into this rank's `down` buffer
+              -> B3 -> combine: out[t] = sum_k w[t,k] * down row read from its owner
+    backward  combine backward: w-scaled gradient rows pushed into the owners' `gdown`,
+              routing-weight gradients from the owners' `down` rows
+              -> B4 -> expert backward (fused dgrad + SwiGLU backward, wgrads)
+              -> `dgrad` buffer -> B5 -> dispatch backward: pull and sum over k
+
+The barriers Bi are device-side (``moe_ep_barrier``). Waits are bounded, and every buffer
+reuse across ranks is ordered by one of them. For example, a rank's next dispatch into a
+peer's receive buffer waits at B1 until that peer's backward has finished reading it.
+
+Results equal the single-GPU layer on the concatenated tokens bit for bit. An expert sees
+its rows in the same order (source rank, then stable slot order), and combine and its
+backward use the unpermute kernels' rounding.
+
+The transport is an interface, so that the data path can be tested with W ranks emulated
+in one process on one GPU. The real one, ``NVLinkTransport``, maps the peers' buffers
+through CUDA IPC (plain device memory, no multicast object).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+_KINDS = ("recv", "down", "gdown", "dgrad")
+
+
+def _as_tensor(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    """A torch view of device memory this library allocated (zero copy, not owned)."""
+    code = {2: "<i2", 4: "<f4", 8: "<i8"}[torch.empty((), dtype=dtype).element_size()]
+
+    class _Mem:
+        __cuda_array_interface__ = {"shape": tuple(shape), "typestr": code, "data": (ptr, False),
+                                    "version": 3, "strides": None}
+
+    t = torch.as_tensor(_Mem(), device=device)
+    return t if t.dtype == dtype else t.view(dtype)
+
+
+class PeerTransport:
+    """What the peer-memory EP step needs from the ranks around it."""
+
+    rank: int
+    world: int
+    capacity: int          # rows of each row buffer
+    buffers: dict          # kind -> this rank's [capacity, cols] tensor
+    bases: dict            # kind -> device int64 [world]: every rank's buffer, mapped here
+
+    def all_gather_counts(self, counts: torch.Tensor) -> torch.Tensor:
+        """[E] int32 (device) -> [world, E] int32 (device), without a host sync."""
+        raise NotImplementedError
+
+    def barrier(self) -> None:
+        raise NotImplementedError
+
+
+class NVLinkTransport(PeerTransport):
+    """One process per GPU. Row buffers and barrier flags live in this library's
+    allocations. The peers map them through CUDA IPC once, so every later step only
+    launches kernels."""
+
+    def __init__(self, group, capacity: int, cols: int, dtype: torch.dtype, device,
+                 timeout_s: float = 5.0):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.capacity, self.cols, self.dtype = capacity, cols, dtype
+        self.device = torch.device(device)
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.epoch = 0
+        lib = _lib.load()
+        es = torch.empty((), dtype=dtype).element_size()
+        sizes = [capacity * cols * es] * len(_KINDS) + [8 * self.world]
+        self._own, handles = [], bytearray()
+        with torch.cuda.device(self.device):
+            for nbytes in sizes:
+                ptr = ctypes.c_void_p()
+                h = (ctypes.c_uint8 * 64)()
+                _lib.check(lib.moe_ipc_malloc(nbytes, ctypes.byref(ptr), ctypes.addressof(h)),
+                           "moe_ipc_malloc")
+                self._own.append(ptr.value)
+                handles += bytes(h)
+            mine = torch.frombuffer(handles, dtype=torch.uint8).to(self.device)
+            allh = torch.empty(self.world, mine.numel(), dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(allh, mine, group=group)
+            allh = allh.cpu()
+            self._opened = []
+            table = [[0] * self.world for _ in sizes]
+            for r in range(self.world):
+                for i in range(len(sizes)):
+                    if r == self.rank:
+                        table[i][r] = self._own[i]
+                        continue
+                    h = (ctypes.c_uint8 * 64).from_buffer_copy(bytes(allh[r, 64 * i: 64 * (i + 1)].tolist()))
+                    ptr = ctypes.c_void_p()
+                    _lib.check(lib.moe_ipc_open(ctypes.addressof(h), ctypes.byref(ptr)), "moe_ipc_open")
+                    self._opened.append(ptr.value)
+                    table[i][r] = ptr.value
+            self.buffers = {k: _as_tensor(self._own[i], (capacity, cols), dtype, self.device)
+                            for i, k in enumerate(_KINDS)}
+            self.bases = {k: torch.tensor(table[i], dtype=torch.int64, device=self.device)
+                          for i, k in enumerate(_KINDS)}
+            self._flags = _as_tensor(self._own[-1], (self.world,), torch.int64, self.device)
+            self._flags.zero_()
+            self._flag_table = torch.tensor(table[-1], dtype=torch.int64, device=self.device)
+            self._status = torch.ones(1, dtype=torch.int32, device=self.device)
+            torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)  # every rank's flags are zero before the first signal
+
+    def all_gather_counts(self, counts):
+        out = torch.empty(self.world, counts.numel(), dtype=counts.dtype, device=counts.device)
+        dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
+        return out
+
+    def barrier(self):
+        self.epoch += 1
+        lib = _lib.load()
+        st = lib.moe_ep_barrier(_lib.ptr(self._flag_table), self.rank, self.world, self.epoch,
+                                self.timeout_ns, _lib.ptr(self._status),
+                                _lib.stream_of(self._flag_table))
+        _lib.check(st, "moe_ep_barrier")
+        _lib.count_launches(1)
+
+    def barrier_ok(self) -> bool:
+        """False if any barrier so far gave up waiting (reads the status: syncs)."""
+        return bool(self._status.item())
+
+    def close(self):
+        torch.cuda.synchronize(self.device)
+        lib = _lib.load()
+        for p in self._opened:
+            lib.moe_ipc_close(p)
+        for p in self._own:
+            lib.moe_ipc_free(p)
+        self._opened, self._own = [], []
+
+
+def _layout(counts_all: torch.Tensor, offsets: torch.Tensor, rank: int, world: int):
+    """From all ranks' per-expert counts [W, E]: delta[E] (this rank's rows of expert e
+    move from offsets[e] to their row in the owner's receive buffer) and this rank's
+    grouped-GEMM offsets [El + 1]."""
+    W, E = counts_all.shape
+    El = E // W
+    cm = counts_all.view(W, W, El).to(torch.int64)            # [src, owner, local expert]
+    tot = cm.sum(0)                                           # [owner, El]
+    recv_base = torch.cumsum(tot, 1) - tot                    # [owner, El]
+    src_off = torch.cumsum(cm, 0) - cm                        # [src, owner, El]
+    delta = (recv_base + src_off[rank]).reshape(E) - offsets[:-1].to(torch.int64)
+    off_local = torch.zeros(El + 1, dtype=torch.int32, device=counts_all.device)
+    off_local[1:] = torch.cumsum(tot[rank], 0).to(torch.int32)
+    return delta.to(torch.int32), off_local
+
+
+class _PeerExperts(torch.autograd.Function):
+    """The expert segment of an EP layer over peer memory:
+    (x [T, d], routing weights [T, K], indices [T, K], local expert weights) -> out [T, d]."""
+
+    @staticmethod
+    def forward(ctx, x, weights, indices, w_gate, w_up, w_down, tr, num_experts):
+        from .gate_up_ops import gmm_gate_up_fwd_raw
+        from .grouped_gemm_ops import _gmm_call
+        from .permute_ops import permute_countsort
+
+        lib = _lib.load()
+        T, d = x.shape
+        K = indices.shape[1]
+        E, W = num_experts, tr.world
+        El = E // W
+        x = x.contiguous()
+        indices = indices.to(torch.int32).contiguous()
+        _, rid, offsets = permute_countsort(x[:, :0], indices, 0, E)   # index pass only
+        counts_all = tr.all_gather_counts(offsets[1:] - offsets[:-1])
+        delta, off_local = _layout(counts_all, offsets, tr.rank, W)
+        ranks = torch.empty(T * K, dtype=torch.int32, device=x.device)
+        rows = torch.empty_like(ranks)
+        stream = _lib.stream_of(x)
+        _lib.check(lib.moe_ep_slot_map(_lib.ptr(indices), _lib.ptr(rid), _lib.ptr(delta), T, K, E,
+                                       El, W, tr.capacity, _lib.ptr(ranks), _lib.ptr(rows), stream),
+                   "moe_ep_slot_map")
+        dt = _lib.dtype_code(x.dtype)
+        tr.barrier()                                               # B1
+        _lib.check(lib.moe_ep_dispatch(_lib.ptr(x), dt, _lib.ptr(tr.bases["recv"]), _lib.ptr(ranks),
+                                       _lib.ptr(rows), T, K, d, stream), "moe_ep_dispatch")
+        tr.barrier()                                               # B2
+        recv, down = tr.buffers["recv"], tr.buffers["down"]
+        gate, up, h = gmm_gate_up_fwd_raw(recv, w_gate, w_up, off_local, True)
+        _gmm_call("moe_gmm_fwd", h, w_down, down, off_local, tr.capacity, w_down.shape[1],
+                  w_down.shape[2], El, True)
+        tr.barrier()                                               # B3
+        out = torch.empty(T, d, device=x.device, dtype=x.dtype)
+        w = weights.contiguous()
+        _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["down"]), dt, _lib.ptr(ranks), _lib.ptr(rows),
+                                      _lib.ptr(w), _lib.dtype_code(w.dtype), T, K, d, _lib.ptr(out),
+                                      stream), "moe_ep_combine")
+        _lib.count_launches(4)
+        ctx.save_for_backward(w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down)
+        ctx.tr, ctx.shape = tr, (T, K, d, El)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        from .gate_up_ops import gmm_dgrad_swiglu_bwd_raw
+        from .grouped_gemm_ops import _gmm_call, gmm_bwd_B_raw, gmm_dgrad_raw
+
+        w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down = ctx.saved_tensors
+        tr = ctx.tr
+        T, K, d, El = ctx.shape
+        lib = _lib.load()
+        grad_out = grad_out.to(w_down.dtype).contiguous()
+        stream = _lib.stream_of(grad_out)
+        dt = _lib.dtype_code(grad_out.dtype)
+        grad_w = torch.empty_like(w)
+        _lib.check(lib.moe_ep_combine_bwd(_lib.ptr(grad_out), _lib.ptr(tr.bases["down"]),
+                                          _lib.ptr(tr.bases["gdown"]), dt, _lib.ptr(ranks),
+                                          _lib.ptr(rows), _lib.ptr(w), _lib.dtype_code(w.dtype), T, K,
+                                          d, _lib.ptr(grad_w), stream), "moe_ep_combine_bwd")
+        tr.barrier()                                               # B4
+        recv, gdown, dgrad = tr.buffers["recv"], tr.buffers["gdown"], tr.buffers["dgrad"]
+        dgate, dup = gmm_dgrad_swiglu_bwd_raw(gdown, w_down, gate, up, off_local, True)
+        g_down = gmm_bwd_B_raw(h, w_down, off_local, gdown, True)
+        _gmm_call("moe_gmm_dgrad", dgate, w_gate, dgrad, off_local, tr.capacity, w_gate.shape[1],
+                  w_gate.shape[2], El, True)
+        dgrad_up = gmm_dgrad_raw(dup, w_up, off_local, True)
+        _lib.check(lib.moe_add_rows(_lib.ptr(dgrad), _lib.ptr(dgrad_up), _lib.ptr(off_local[El:]),
+                                    tr.capacity, d, dt, stream), "moe_add_rows")
+        g_gate = gmm_bwd_B_raw(recv, w_gate, off_local, dgate, True)
+        g_up = gmm_bwd_B_raw(recv, w_up, off_local, dup, True)
+        tr.barrier()                                               # B5
+        grad_x = torch.empty(T, d, device=grad_out.device, dtype=grad_out.dtype)
+        _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["dgrad"]), dt, _lib.ptr(ranks), _lib.ptr(rows),
+                                      None, 0, T, K, d, _lib.ptr(grad_x), stream), "moe_ep_combine")
+        _lib.count_launches(3)
+        return grad_x, grad_w, None, g_gate, g_up, g_down, None, None
+
+
+def peer_experts(x, weights, indices, w_gate, w_up, w_down, transport: PeerTransport,
+                 num_experts: int) -> torch.Tensor:
+    """The EP expert segment over peer memory (differentiable in x, weights and the local
+    expert weights): out[t] = sum_k weights[t,k] * expert_{indices[t,k]}(x[t])."""
+    return _PeerExperts.apply(x, weights, indices, w_gate, w_up, w_down, transport, num_experts)
+
+
+def capacity_rows(tokens_per_rank: int, top_k: int, world: int) -> int:
+    """Receive-buffer rows for the worst case: every slot of every rank on one rank."""
+    return tokens_per_rank * top_k * world
