@@ -182,8 +182,34 @@ class EPMoELayer(torch.nn.Module):
         # cfg4: 2 chunks win at 2 ranks (16.26 vs 16.49 ms) but lose at 8 (15.45 vs 14.2 ms,
         # the per-chunk GEMMs get too small), so the default is the plain sequence.
         self.chunks = 0
+        # "nccl": dispatch / combine as NCCL all-to-alls (the tested default at every world
+        # size); "nvlink": straight over peer memory (ep_peer.py), no host sync in the step.
+        # The peer path needs the same token count on every rank.
+        self.transport = "nccl"
+        self._peer = None
+
+    def _forward_peer(self, x):
+        from .ep_peer import NVLinkTransport, capacity_rows, peer_experts
+        from .fused_topk_softmax_ops import fused_topk_softmax
+
+        world = dist.get_world_size(self.group)
+        cap = capacity_rows(x.shape[0], self.top_k, world)
+        if self._peer is None or self._peer.capacity < cap or self._peer.cols != x.shape[1]:
+            if self._peer is not None:
+                self._peer.close()
+            self._peer = NVLinkTransport(self.group, cap, x.shape[1], x.dtype, x.device)
+        logits = x @ self.w_router.t()
+        if self.router_bias is not None:
+            logits = logits + self.router_bias
+        if self.fp32_routing:
+            logits = logits.float()
+        weights, indices = fused_topk_softmax(logits, self.top_k)
+        return peer_experts(x, weights, indices, self.w_gate, self.w_up, self.w_down, self._peer,
+                            self.num_experts)
 
     def forward(self, x):
+        if self.transport == "nvlink":
+            return self._forward_peer(x)
         if self.chunks > 0:
             return ep_moe_forward_overlapped(x, self.w_router, self.w_gate, self.w_up, self.w_down,
                                              self.top_k, self.num_experts, group=self.group,
