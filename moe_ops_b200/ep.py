@@ -207,6 +207,13 @@ class EPMoELayer(torch.nn.Module):
         return peer_experts(x, weights, indices, self.w_gate, self.w_up, self.w_down, self._peer,
                             self.num_experts)
 
+    def close(self):
+        """Releases the peer-memory buffers (collective when they exist: every rank calls
+        it).  Tensors viewing them must not be used afterwards."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
     def forward(self, x):
         if self.transport == "nvlink":
             return self._forward_peer(x)
