@@ -142,10 +142,17 @@ class NVLinkTransport(PeerTransport):
         return bool(self._status.item())
 
     def close(self):
+        """Collective: unmaps the peers' buffers, waits until every rank has done so, then
+        frees this rank's own (an exporter must not free memory a peer still maps)."""
+        if not self._own:
+            return
         torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         lib = _lib.load()
         for p in self._opened:
             lib.moe_ipc_close(p)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
         for p in self._own:
             lib.moe_ipc_free(p)
         self._opened, self._own = [], []
