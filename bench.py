@@ -208,9 +208,10 @@ def run_ours(args):
 
         layer = EPMoELayer(d, E, K, H, fp32_routing=cfg["fp32_routing"], device=dev,
                            dtype=torch.bfloat16)
-        # auto: peer memory at 2 ranks, where it is validated (bit-exact against the single-GPU
-        # layer, and 6.5 % faster than NCCL on cfg4); NCCL at larger worlds until validated.
-        layer.transport = (("nvlink" if world == 2 else "nccl") if args.ep_transport == "auto"
+        # auto: peer memory up to 4 ranks, where it has run bit-exact against the single-GPU
+        # layer on real GPUs (and measured 6.5 % faster than NCCL on cfg4 at 2 ranks); NCCL
+        # at 8 ranks until the peer path has run there.
+        layer.transport = (("nvlink" if world <= 4 else "nccl") if args.ep_transport == "auto"
                            else args.ep_transport)
         args.ep_transport = layer.transport
         with torch.no_grad():
@@ -545,7 +546,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--ep-transport", choices=["auto", "nccl", "nvlink"], default="auto",
                     help="N > 1: dispatch / combine as NCCL all-to-alls, or over NVLink peer "
-                         "memory; auto = nvlink at 2 ranks, nccl above")
+                         "memory; auto = nvlink up to 4 ranks, nccl above")
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
