@@ -239,8 +239,10 @@ int moe_add_rows(void* dst, const void* src, const int32_t* n_rows, int64_t max_
 /* Cross-GPU barrier on `world` int64 flag arrays of `world` slots each (one per rank, in
  * IPC memory): writes `epoch` to slot `rank` of every rank's array (after a system-scope
  * fence), then waits until every slot of this rank's array reaches `epoch`.  Gives up after
- * timeout_ns: *status (device int32, may be NULL) = 0 and device error 4; else 1.  Epochs
- * must increase by one per barrier.  The ranks must run on different GPUs. */
+ * timeout_ns: *status (device int32, may be NULL) = 0 and device error 4; a barrier that
+ * completes leaves *status unchanged, so one status word records any failure over many
+ * barriers.  Epochs must increase by one per barrier.  The ranks must run on different
+ * GPUs. */
 int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t epoch,
                    uint64_t timeout_ns, int32_t* status, void* stream);
 

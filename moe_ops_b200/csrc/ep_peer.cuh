@@ -54,8 +54,9 @@ ep_slot_map_kernel(const int32_t* __restrict__ indices, const int32_t* __restric
 // One warp.  Lane i < world: make this rank's earlier writes visible system-wide, then
 // store `epoch` into slot `me` of rank i's flag array (a peer store over NVLink, or a local
 // one for i == me).  Then lane i waits until slot i of this rank's own array reaches
-// `epoch`, giving up after timeout_ns (device error 4, *status = 0).  Epochs increase by one
-// per barrier, so a flag never needs resetting.
+// `epoch`, giving up after timeout_ns (device error 4, *status = 0; a barrier that completes
+// leaves *status as it was, so a failure stays visible).  Epochs increase by one per
+// barrier, so a flag never needs resetting.
 __global__ void ep_barrier_kernel(int64_t* const* __restrict__ flags, int me, int world,
                                   int64_t epoch, uint64_t timeout_ns, int32_t* __restrict__ status) {
   const int lane = threadIdx.x;
@@ -79,9 +80,9 @@ __global__ void ep_barrier_kernel(int64_t* const* __restrict__ flags, int me, in
     }
   }
   const bool all_ok = __all_sync(0xffffffffu, ok);
-  if (lane == 0) {
-    if (!all_ok) raise_device_error(4);
-    if (status != nullptr) *status = all_ok ? 1 : 0;
+  if (lane == 0 && !all_ok) {
+    raise_device_error(4);
+    if (status != nullptr) *status = 0;
   }
   __threadfence_system();
 }

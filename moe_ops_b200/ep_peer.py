@@ -215,7 +215,7 @@ class _PeerExperts(torch.autograd.Function):
         _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["down"]), dt, _lib.ptr(ranks), _lib.ptr(rows),
                                       _lib.ptr(w), _lib.dtype_code(w.dtype), T, K, d, _lib.ptr(out),
                                       stream), "moe_ep_combine")
-        _lib.count_launches(4)
+        _lib.count_launches(3)
         ctx.save_for_backward(w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down)
         ctx.tr, ctx.shape = tr, (T, K, d, El)
         return out

@@ -165,8 +165,8 @@ def test_barrier_gives_up_on_a_silent_peer(cuda_dev):
     lib = _lib.load()
     flags = [torch.zeros(2, dtype=torch.int64, device=cuda_dev) for _ in range(2)]
     table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=cuda_dev)
-    status = torch.full((1,), 7, dtype=torch.int32, device=cuda_dev)
-    # One rank alone: its own signal satisfies it.
+    status = torch.ones(1, dtype=torch.int32, device=cuda_dev)
+    # One rank alone: its own signal satisfies it, and the status stays 1.
     one = torch.tensor([flags[0].data_ptr()], dtype=torch.int64, device=cuda_dev)
     assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, 1, 50_000_000, _lib.ptr(status), None) == 0
     assert status.item() == 1
@@ -175,6 +175,9 @@ def test_barrier_gives_up_on_a_silent_peer(cuda_dev):
     assert status.item() == 0
     assert flags[1][0].item() == 1  # its own signal reached the silent peer's array
     assert _lib.read_device_error() == 4
+    # A later barrier that completes leaves the failure recorded.
+    assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, 2, 50_000_000, _lib.ptr(status), None) == 0
+    assert status.item() == 0
 
 
 def _free_port():
