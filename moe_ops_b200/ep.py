@@ -1,4 +1,5 @@
-"""Expert parallelism (EP) for the SwiGLU MoE layer over NCCL.
+"""Expert parallelism (EP) for the SwiGLU MoE layer: the NCCL transport, and the layer
+class that can also run the NVLink peer-memory transport of ep_peer.py.
 
 The reference has no distributed code (tests/test_moe.py:1-9: "no distributed comms");
 this is the B200 extension its benchmark configs 4-5 ask for.  Rank r of W owns experts
@@ -12,7 +13,8 @@ this is the B200 extension its benchmark configs 4-5 ask for.  Rank r of W owns 
   4. all_to_all of rows (differentiable; backward is the reverse exchange);
   5. regroup the received rows (source-rank-major) to local-expert-major with the same
      counting-sort permute (K=1), giving the local grouped-GEMM offsets;
-  6. gate / up grouped GEMMs, SwiGLU, down grouped GEMM on the local experts;
+  6. the SwiGLU expert MLP on the local experts (gate/up + SwiGLU in one launch, then the
+     down GEMM);
   7. undo the regroup (permute_backward, an exact gather), all_to_all back;
   8. unpermute weighted by the routing probabilities.
 
