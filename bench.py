@@ -11,8 +11,14 @@ unpermute, then the full backward (6 grouped GEMMs, unpermute/permute/top-k back
 `value` is grouped-GEMM TFLOP/s of the whole job (9 GEMMs per step, 2*T*K*d*H FLOPs each).
 Inputs (17.3 GB of weights) are far larger than L2, so no flush is needed between steps.
 Under torchrun (N > 1) the layer is expert-parallel (moe_ops_b200.ep): each rank holds
-E/N experts and its own 8192 tokens, tokens go to their experts' ranks and back through
-NCCL all-to-alls (weak scaling: per-rank work is fixed as N grows).
+E/N experts and 8192/N of the tokens (strong scaling, as config 4 is written), and rows go
+to their experts' ranks and back over NVLink peer memory (--ep-transport nccl: NCCL
+all-to-alls).  Before timing, an N > 1 run checks the EP layer over the same transport on
+a small problem against the single-GPU layer and the CPU oracle ("ep_parity"), and exits
+non-zero if that fails; after timing it reads the device error word and the peer barriers'
+status ("device_error", "peer_barriers_ok") and exits non-zero if either is set.
+At N = 1 the line also carries per-op figures ("ops": config 2 grouped GEMMs beside torch
+grouped_mm and the reference's own Triton grouped GEMM, config 3 routing primitives).
 
 `--impl reference` times the reference's PyTorch-native CPU path (restated in oracle/)
 on the host cores, on a bounded sample of the same workload (8 of the 64 experts with
@@ -33,10 +39,17 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 CONFIGS = {
-    # BASELINE config 4 (the headline): every rank holds 8192 tokens (weak scaling).
+    # BASELINE config 4 (the headline): 8192 tokens in total, split evenly over the ranks
+    # (strong scaling, as the config is written).
     "cfg4": dict(tokens=8192, d_model=4096, experts=64, top_k=2, hidden=11008, fp32_routing=False,
-                 zipf=False, global_tokens=False, router_std=0.02,
-                 workload="cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16"),
+                 zipf=False, global_tokens=True, router_std=0.02,
+                 workload="cfg4 SwiGLU MoE layer fwd+bwd, T=8192 (in total) d=4096 E=64 topK=2 "
+                          "H=11008 bf16"),
+    # Not a BASELINE config: cfg4's layer with 8192 tokens on every rank (weak scaling).
+    "cfg4-weak": dict(tokens=8192, d_model=4096, experts=64, top_k=2, hidden=11008,
+                      fp32_routing=False, zipf=False, global_tokens=False, router_std=0.02,
+                      workload="cfg4 layer with 8192 tokens PER RANK (weak scaling; not the "
+                               "BASELINE config), d=4096 E=64 topK=2 H=11008 bf16"),
     # 32768 tokens in total split over the ranks (strong scaling), router
     # logits ~ N(0, 1) plus a Zipf bias 1.5*log(1/rank^1.2) over a random expert order.
     "cfg5": dict(tokens=32768, d_model=7168, experts=256, top_k=8, hidden=2048, fp32_routing=True,
@@ -173,6 +186,89 @@ def _make_inputs(dev, T, d, seed):
     return x, go
 
 
+def ep_parity_check(world, rank, dev, transport, T=512, d=256, K=2, H=512, tol=1e-2):
+    """Before the timed region of an N > 1 run: the expert-parallel layer, over the transport
+    the run times, on a small seeded problem (T tokens per rank, E = 4*N experts), against
+    the single-GPU layer over all ranks' tokens on this GPU (output, x, router and expert
+    weight gradients), and on rank 0 the layer output against the CPU oracle
+    (oracle.moe_oracle, fp32; the checker, never the timed path).  Returns
+    {"max_rel_err", "ok", "checks"}; the errors are maxima over ranks."""
+    import torch.distributed as dist
+
+    from moe_ops_b200 import _lib
+    from moe_ops_b200.ep import EPMoELayer
+    from moe_ops_b200.moe_layer import MoELayer
+
+    E = 4 * world
+    el = E // world
+    g = torch.Generator().manual_seed(2024)
+    xs = [torch.randn(T, d, generator=g).bfloat16() for _ in range(world)]
+    gos = [torch.randn(T, d, generator=g).bfloat16() for _ in range(world)]
+    wr = (torch.randn(E, d, generator=g) * 0.5).bfloat16()
+    wg, wu = ((torch.randn(E, H, d, generator=g) * 0.05).bfloat16() for _ in range(2))
+    wd = (torch.randn(E, d, H, generator=g) * 0.05).bfloat16()
+    sl = slice(rank * el, (rank + 1) * el)
+
+    ep = EPMoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16)
+    ep.transport = transport
+    with torch.no_grad():
+        ep.w_router.copy_(wr)
+        for p, w in ((ep.w_gate, wg), (ep.w_up, wu), (ep.w_down, wd)):
+            p.copy_(w[sl])
+    x = xs[rank].to(dev).requires_grad_(True)
+    out = ep(x)
+    out.backward(gos[rank].to(dev))
+    torch.cuda.synchronize()
+    healthy = ep.health_ok()
+    ep.close()
+    g_router = ep.w_router.grad.float().clone()
+    dist.all_reduce(g_router)  # the router is replicated: its gradient sums over ranks
+
+    full = MoELayer(d, E, K, H, device=dev, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p, w in ((full.w_router, wr), (full.w_gate, wg), (full.w_up, wu), (full.w_down, wd)):
+            p.copy_(w)
+    xa = torch.cat(xs).to(dev).requires_grad_(True)
+    ref = full(xa)
+    ref.backward(torch.cat(gos).to(dev))
+    rows = slice(rank * T, (rank + 1) * T)
+
+    def rel(a, b):
+        a, b = a.detach().double().cpu(), b.detach().double().cpu()
+        return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+    errs = {"out": rel(out, ref[rows]), "grad_x": rel(x.grad, xa.grad[rows]),
+            "grad_router": rel(g_router, full.w_router.grad.float()),
+            "grad_w_gate": rel(ep.w_gate.grad, full.w_gate.grad[sl]),
+            "grad_w_up": rel(ep.w_up.grad, full.w_up.grad[sl]),
+            "grad_w_down": rel(ep.w_down.grad, full.w_down.grad[sl])}
+    if rank == 0:
+        from oracle.moe_oracle import moe_layer_forward
+        import moe_ops_b200 as M
+
+        w_, idx = M.fused_topk_softmax(xa.detach() @ full.w_router.detach().t(), K)
+        o = moe_layer_forward(xa.detach().cpu().float(), wr.float(), wg.float(), wu.float(),
+                              wd.float(), K, E, routing=(w_.cpu().float(), idx.cpu()))
+        errs["out_vs_oracle"] = rel(ref, o)
+    names = sorted(errs)
+    t = torch.tensor([errs.get(n, 0.0) for n in names] + [0.0 if healthy else 1.0,
+                                                          float(_lib.read_device_error())],
+                     device=dev, dtype=torch.float64)
+    # rank 0 alone has the oracle entry; every rank has the others
+    allt = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(allt, t)
+    mx = torch.stack(allt).max(0).values.tolist()
+    checks = {n: float(f"{v:.3e}") for n, v in zip(names, mx[:len(names)])}
+    bad = mx[len(names)] > 0 or mx[len(names) + 1] > 0
+    worst = max(checks.values())
+    del full, ep
+    torch.cuda.empty_cache()
+    return {"max_rel_err": float(f"{worst:.3e}"), "ok": bool(worst < tol and not bad),
+            "tolerance": tol, "checks": checks, "transport": transport,
+            "problem": f"{T} tokens/rank, d={d}, E={E}, K={K}, H={H}, bf16",
+            "barrier_or_device_error": bool(bad)}
+
+
 def run_ours(args):
     import torch.distributed as dist
 
@@ -195,6 +291,7 @@ def run_ours(args):
         cfg = dict(cfg, workload=cfg["workload"] + f" [slice: E={E}, T={T}]")
     router_std = cfg["router_std"] or d ** -0.5  # None: logits ~ N(0, 1)
 
+    parity = None
     if world == 1:
         layer = MoELayer(d, E, K, H, fp32_routing=cfg["fp32_routing"], device=dev,
                          dtype=torch.bfloat16)
@@ -206,14 +303,19 @@ def run_ours(args):
         # Expert parallelism: this rank holds E/world experts, the router is replicated.
         from moe_ops_b200.ep import EPMoELayer
 
+        transport = args.ep_transport if args.ep_transport != "auto" else "nvlink"
+        args.ep_transport = transport
+        # Correctness of the multi-GPU layer, over the same transport, before timing it.
+        parity = ep_parity_check(world, rank, dev, transport)
+        if not parity["ok"]:
+            if rank == 0:
+                print(json.dumps({"metric": METRIC, "error": "ep parity check failed",
+                                  "ep_parity": parity}), flush=True)
+            dist.destroy_process_group()
+            sys.exit(3)
         layer = EPMoELayer(d, E, K, H, fp32_routing=cfg["fp32_routing"], device=dev,
                            dtype=torch.bfloat16)
-        # auto: peer memory up to 4 ranks, where it has run bit-exact against the single-GPU
-        # layer on real GPUs (and measured 6.5 % faster than NCCL on cfg4 at 2 ranks); NCCL
-        # at 8 ranks until the peer path has run there.
-        layer.transport = (("nvlink" if world <= 4 else "nccl") if args.ep_transport == "auto"
-                           else args.ep_transport)
-        args.ep_transport = layer.transport
+        layer.transport = transport
         with torch.no_grad():
             gen = torch.Generator(device=dev).manual_seed(1234 + rank)
             for w in (layer.w_gate, layer.w_up, layer.w_down):
@@ -235,7 +337,7 @@ def run_ours(args):
         xin = xin.detach().requires_grad_(True)
         out = layer(xin)
         out.backward(gin)
-        return out
+        return out, xin
 
     def barrier():
         if world > 1:
@@ -245,6 +347,7 @@ def run_ours(args):
     for _ in range(max(args.warmup, 3)):
         step(x, grad_out)
     barrier()
+    torch.cuda.reset_peak_memory_stats(dev)
 
     # ------------------------------------------------------------ device-timed region
     sampler = ClockSampler(local)
@@ -263,58 +366,89 @@ def run_ours(args):
     launches = _lib.launch_count - launches0
     timing, _lib.gemm_timing = _lib.gemm_timing, None
     gemm_ms = sum(t[1].elapsed_time(t[2]) for t in timing)
-    gemm_flops = sum(t[3] for t in timing)
+    # The grouped GEMMs' FLOPs from the rows the experts actually computed on: T*K on one
+    # GPU; under EP the rows this rank received (the peer transport's GEMM calls are sized
+    # for its worst-case buffers, so their nominal row counts would overstate the work).
+    live_rows = T * K if world == 1 else layer.local_rows()
+    gemm_flops = 9 * 2.0 * live_rows * d * H * args.steps
     # Per-launch roofline time: max(FLOPs / tensor peak, DRAM bytes / copy bandwidth,
-    # written bytes / write bandwidth measured now on this GPU).
+    # written bytes / write bandwidth measured now on this GPU), rows scaled to the live ones.
     peaks_, _ = _peaks()
     write_gbs = _write_bandwidth(dev)
     t_roof = 0.0
+    nominal = sum(t[3] for t in timing)
+    scale = gemm_flops / nominal if nominal else 1.0
     for t in timing:
-        flop_s = t[3] / (peaks_.get("bf16_tflops_sustained", 1400.0) * 1e12)
+        flop_s = t[3] * scale / (peaks_.get("bf16_tflops_sustained", 1400.0) * 1e12)
         mem_s = max((t[4] + t[5]) / (peaks_["hbm_gbs"] * 1e9), t[5] / (write_gbs * 1e9))
         t_roof += max(flop_s, mem_s)
+    peak_mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
 
     # ------------------------------------------------------------ end to end (host buffers)
+    # Every step: the activations and the output gradient come from pinned host memory, and
+    # the layer output and the input gradient go back to pinned host memory.
     x_host = x.cpu().pin_memory()
     g_host = grad_out.cpu().pin_memory()
-    res_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    gx_host = torch.empty_like(x_host).pin_memory()
     x_dev = torch.empty_like(x)
     g_dev = torch.empty_like(grad_out)
 
-    copy_stream = torch.cuda.Stream(device=dev)
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
 
     def e2e_step():
-        # The activations are copied on the compute stream (the forward needs them first);
-        # the output gradient is copied on a copy stream while the forward runs, and the
-        # backward waits for it.  Both copies happen every step.
+        # The activations are copied on the compute stream (the forward needs them first).
+        # The output gradient comes in on a copy stream while the forward runs; the output
+        # goes back on a second copy stream while the backward runs, and the input gradient
+        # while the next step's forward runs.  Every copy happens every step.
         main = torch.cuda.current_stream(dev)
         x_dev.copy_(x_host, non_blocking=True)
-        copy_stream.wait_stream(main)  # the previous step's backward has read g_dev
-        with torch.cuda.stream(copy_stream):
+        h2d.wait_stream(main)  # the previous step's backward has read g_dev
+        with torch.cuda.stream(h2d):
             g_dev.copy_(g_host, non_blocking=True)
         for p in layer.parameters():
             p.grad = None
         xin = x_dev.detach().requires_grad_(True)
         out = layer(xin)
-        main.wait_stream(copy_stream)
+        d2h.wait_stream(main)
+        with torch.cuda.stream(d2h):
+            out_host.copy_(out.detach(), non_blocking=True)
+        out.record_stream(d2h)
+        main.wait_stream(h2d)
         out.backward(g_dev)
-        res_host.copy_(out.detach().float().sum().reshape(1), non_blocking=True)
+        d2h.wait_stream(main)
+        with torch.cuda.stream(d2h):
+            gx_host.copy_(xin.grad, non_blocking=True)
+        xin.grad.record_stream(d2h)
 
     e2e_step()
+    torch.cuda.current_stream(dev).wait_stream(d2h)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         e2e_step()
+    torch.cuda.current_stream(dev).wait_stream(d2h)  # the last copies back are inside
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
 
-    # max over ranks
-    t = torch.tensor([ms_total, e2e_ms], device=dev, dtype=torch.float64)
+    # Device-side health after both timed regions: the library's error word (a bounded
+    # wait that gave up, a refused slot) and, under EP, the peer barriers' status.
+    dev_err = _lib.read_device_error()
+    healthy = layer.health_ok() if world > 1 else True
+
+    # max over ranks (times, errors); every rank's live rows
+    t = torch.tensor([ms_total, e2e_ms, float(dev_err), 0.0 if healthy else 1.0, peak_mem_gb],
+                     device=dev, dtype=torch.float64)
+    rows_all = [live_rows]
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms = t.tolist()
+        gath = [None] * world
+        dist.all_gather_object(gath, live_rows)
+        rows_all = gath
+    ms_total, e2e_ms, dev_err, unhealthy, peak_mem_gb = t.tolist()
     ms_step = ms_total / args.steps
     value = flops_step * world / (ms_step * 1e-3) / 1e12
     e2e_value = flops_step * world / (e2e_ms / args.steps * 1e-3) / 1e12
@@ -323,6 +457,7 @@ def run_ours(args):
     achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
     peak = peaks.get("bf16_tflops_sustained", 1400.0)
     traffic = _traffic_per_launch()
+    ep_label = f"ep{world}" if world > 1 else "single"
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -339,11 +474,12 @@ def run_ours(args):
         "config": {
             "workload": cfg["workload"],
             "model": "moe_layer_swiglu", "global_batch": T * world, "seq_len": 1,
-            "parallelism": f"ep{world}" if world > 1 else "single",
+            "parallelism": ep_label,
             "ep_transport": args.ep_transport if world > 1 else None,
             "tokens_per_rank": T,
-            "l2": "inputs larger than L2 (expert weights 17.3 GB cfg4 / 22.5 GB cfg5), no flush",
-            "gemm_flops_per_step": flops_step,
+            "l2": "inputs larger than L2 (expert weights 17.3 GB cfg4 / 22.5 GB cfg5 in total), "
+                  "no flush",
+            "gemm_flops_per_step": flops_step * world,
         },
         "roofline": {
             "bound": "tensor",
@@ -353,11 +489,14 @@ def run_ours(args):
             "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4) if achieved else None,
             "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
+            "live_rows_per_rank": rows_all,
             "gemm_share_of_step": round(gemm_ms / ms_total, 4) if ms_total else None,
             "gemm_time_vs_roofline": round(t_roof * 1e3 / gemm_ms, 4) if gemm_ms else None,
-            "roofline_note": "frac = achieved / tensor peak; gemm_time_vs_roofline = sum over "
-                             "launches of max(FLOP/tensor peak, DRAM bytes/copy BW, written "
-                             f"bytes/{write_gbs:.0f} GB/s write BW measured in this run) / measured GEMM time",
+            "roofline_note": "achieved = 9 GEMMs x 2*rows*d*H over the rows the experts computed "
+                             "on (rank 0's, live_rows_per_rank[0]) / rank 0's summed GEMM launch "
+                             "time (CUDA events); gemm_time_vs_roofline = sum over launches of "
+                             "max(FLOP/tensor peak, DRAM bytes/copy BW, written bytes/"
+                             f"{write_gbs:.0f} GB/s write BW measured in this run) / GEMM time",
             "traffic": traffic.get("bytes_per_launch") if traffic else None,
             "write_gbs": round(write_gbs, 1),
         },
@@ -365,19 +504,148 @@ def run_ours(args):
             "value": round(e2e_value, 2), "unit": "TFLOP/s",
             "ms_per_step": round(e2e_ms / args.steps, 4),
             "h2d_bytes_per_step": x.numel() * 2 + grad_out.numel() * 2,
-            "d2h_bytes_per_step": 4,
-            "note": "pinned host inputs copied every step: activations before the forward, "
-                    "the output gradient on a copy stream during the forward",
+            "d2h_bytes_per_step": out_host.numel() * 2 + gx_host.numel() * 2,
+            "note": "per rank and step: activations and output gradient copied in from pinned "
+                    "host memory (the gradient on a copy stream during the forward), layer "
+                    "output and input gradient copied back to pinned host memory on a second "
+                    "copy stream (during the backward / the next forward); the last step's "
+                    "copies finish inside the timed region",
         },
         "gpu_launches": launches,
+        "device_error": int(dev_err),
+        "peer_barriers_ok": not unhealthy,
+        "peak_mem_gb_per_rank": round(peak_mem_gb, 2),
         "clocks": clocks,
     }
+    if parity is not None:
+        line["ep_parity"] = parity
+    if rank == 0 and world == 1 and not args.no_ops and args.config == "cfg4" and not args.experts:
+        line["ops"] = ops_block(dev, steps=20, warmup=3)
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "cfg4":
         line["cpu_baseline"] = cpu_baseline(steps=1, warmup=1)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    failed = int(dev_err) != 0 or unhealthy
     if world > 1:
         dist.destroy_process_group()
+    if failed:
+        sys.exit(4)
+
+
+def _cfg2_sizes(zipf: bool):
+    """BASELINE config 2 group sizes: 16 x 1024, or Zipf(s=1.1) sizes summing to 16384 with
+    2 empty experts."""
+    if not zipf:
+        return [1024] * 16
+    w = 1.0 / torch.arange(1, 15).double() ** 1.1
+    sizes = (w / w.sum() * 16384).floor().long().tolist()
+    sizes[0] += 16384 - sum(sizes)
+    return sizes[:7] + [0] + sizes[7:12] + [0] + sizes[12:]
+
+
+def _reference_triton():
+    """The reference package (triton_gmm_ops, installed unchanged into baseline/_ref) for
+    timing its own Triton grouped GEMM on this GPU, or None with the reason."""
+    path = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(path, "triton_gmm_ops")):
+        return None, "baseline/_ref not installed"
+    if path not in sys.path:
+        sys.path.append(path)
+    try:
+        import triton_gmm_ops as tg  # noqa: F401
+        return tg, None
+    except Exception as e:  # noqa: BLE001
+        return None, f"import failed: {e}"[:120]
+
+
+def ops_block(dev, steps=20, warmup=3):
+    """Per-op figures on this GPU, beside the library bars BASELINE names
+    grouped GEMMs (uniform and Zipf; forward, dgrad, wgrad) with torch's grouped_mm and the
+    reference's own Triton grouped GEMM on the same inputs, and the config 3 routing
+    primitives.  GEMM inputs are 0.67 GB (> L2); routing ops are captured in CUDA graphs."""
+    import moe_ops_b200 as M
+    from moe_ops_b200.grouped_gemm_ops import gmm_bwd_B_raw, gmm_dgrad_raw, gmm_fwd_raw
+
+    peaks, kind = _peaks()
+    burst = peaks.get("bf16_tflops", 1590.0)
+    res = {"peak_kind": f"{kind} bf16_tflops (burst: ops timed alone) / hbm_gbs",
+           "bf16_tflops_peak": burst, "hbm_gbs_peak": peaks["hbm_gbs"]}
+    tg, why = _reference_triton()
+    g = torch.Generator(device=dev).manual_seed(7)
+    E, Kd, N = 16, 4096, 4096
+    A = torch.randn(16384, Kd, device=dev, generator=g).to(torch.bfloat16)
+    B = (torch.randn(E, N, Kd, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    gC = torch.randn(16384, N, device=dev, generator=g).to(torch.bfloat16)
+    fl = 2.0 * 16384 * N * Kd
+    for name, zipf in (("cfg2_uniform", False), ("cfg2_zipf", True)):
+        sizes = _cfg2_sizes(zipf)
+        off = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+        off[1:] = torch.tensor(sizes, device=dev).cumsum(0).to(torch.int32)
+        ends = off[1:].contiguous()
+        Bt = B.transpose(1, 2)
+        r = {}
+        fns = {"fwd": lambda: gmm_fwd_raw(A, B, off, True),
+               "dgrad": lambda: gmm_dgrad_raw(gC, B, off, True),
+               "wgrad": lambda: gmm_bwd_B_raw(A, B, off, gC, True),
+               "torch_grouped_mm_fwd": lambda: torch.nn.functional.grouped_mm(A, Bt, offs=ends),
+               "torch_grouped_mm_dgrad": lambda: torch.nn.functional.grouped_mm(gC, B, offs=ends)}
+        if tg is not None:
+            fns["reference_triton_fwd"] = lambda: tg.grouped_gemm(A, B, off, trans_b=True)
+        for k, fn in fns.items():
+            try:
+                ms = _time_events(fn, steps, warmup)
+            except Exception as e:  # noqa: BLE001
+                r[k] = {"error": f"{type(e).__name__}: {e}"[:120]}
+                continue
+            tf = fl / (ms * 1e-3) / 1e12
+            r[k] = {"ms": round(ms, 4), "tflops": round(tf, 1), "frac": round(tf / burst, 4)}
+        res[name] = r
+    if tg is None:
+        res["reference_triton"] = f"not timed: {why}"
+    else:
+        res["reference_triton"] = "triton_gmm_ops.grouped_gemm forward (its sm90+ TMA path, " \
+                                  "autotuned on first call) from baseline/_ref, unchanged"
+    del A, B, gC
+    res["cfg3_routing"] = _routing_ops(dev, steps=max(steps, 50), warmup=warmup)
+    return res
+
+
+def _routing_ops(dev, steps, warmup):
+    """BASELINE config 3 routing primitives (T=8192, d=4096 bf16, E=64, K=2), each captured
+    in a CUDA graph and replayed (GPU time only); GB/s of unique bytes and the fraction of
+    the measured HBM copy bandwidth."""
+    import moe_ops_b200 as M
+
+    peaks, _ = _peaks()
+    g = torch.Generator(device=dev).manual_seed(1)
+    T, d, E, K = 8192, 4096, 64, 2
+    x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(T, E, device=dev, generator=g)
+    w, idx = M.fused_topk_softmax(logits, K)
+    perm, rid, off = M.permute(x, idx, E=E)
+    prob = w.float()
+    gout = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
+    row = T * d * 2
+    cases = {
+        "topk_fwd": (lambda: M.fused_topk_softmax(logits, K), T * E * 4 + T * K * 8),
+        "permute": (lambda: M.permute(x, idx, E=E), row * (1 + K) + T * K * 12),
+        "unpermute_fwd": (lambda: M.unpermute_forward(perm, rid, prob, T, K), row * (1 + K)),
+        "permute_backward": (lambda: M.permute_backward(perm, rid, T, K), row * (1 + K)),
+        "unpermute_bwd": (lambda: M.unpermute_backward(gout, perm, rid, prob, T, K), row * (1 + 2 * K)),
+    }
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        ms = _time_events(graph.replay, steps, warmup)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}
+    return res
 
 
 def cpu_baseline(steps: int = 1, warmup: int = 1, sample_experts: int = 8):
@@ -431,9 +699,9 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": base["value"], "unit": "TFLOP/s", "n_gpus": world,
         "steps": steps, "warmup": warmup, "ms_per_step": round(ms_step, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded)", "impl": "reference",
-        "config": {"workload": "cfg4 SwiGLU MoE layer fwd+bwd, T=8192 d=4096 E=64 topK=2 H=11008 bf16",
+        "config": {"workload": CFG["workload"],
                    "model": "moe_layer_swiglu", "sample": base["sample"]},
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -500,44 +768,20 @@ def run_case(args):
         res.update({"GB/s": round(gbs, 1), "bytes": 5768732672,
                     "frac_of_copy_peak": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": kind})
     elif args.case == "routing":
-        T, d, E, K = 8192, 4096, 64, 2
-        x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
-        logits = torch.randn(T, E, device=dev, generator=g)
-        w, idx = M.fused_topk_softmax(logits, K)
-        perm, rid, off = M.permute(x, idx, E=E)
-        prob = w.float()
-        gout = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
-        row = T * d * 2
-        cases = {
-            "topk_fwd": (lambda: M.fused_topk_softmax(logits, K), T * E * 4 + T * K * 8),
-            "permute": (lambda: M.permute(x, idx, E=E), row * (1 + K) + T * K * 12),
-            "unpermute_fwd": (lambda: M.unpermute_forward(perm, rid, prob, T, K), row * (1 + K)),
-            "permute_backward": (lambda: M.permute_backward(perm, rid, T, K), row * (1 + K)),
-            "unpermute_bwd": (lambda: M.unpermute_backward(gout, perm, rid, prob, T, K), row * (1 + 2 * K)),
-        }
-        for name, (fn, nbytes) in cases.items():
-            # Captured in a CUDA graph and replayed: GPU time only (eager timing of these
-            # short ops would measure the Python/launch path instead).
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                fn()
-            ms = _time_events(graph.replay, args.steps, args.warmup)
-            gbs = nbytes / (ms * 1e-3) / 1e9
-            res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
-                         "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}
+        res.update(_routing_ops(dev, steps=args.steps, warmup=args.warmup))
         res["peak_kind"] = kind
+    elif args.case == "ops":
+        res.update(ops_block(dev, steps=args.steps, warmup=args.warmup))
     print(json.dumps(res), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg4",
-                    help="layer workload: cfg4 (headline, default) or cfg5")
+                    help="layer workload: cfg4 (headline, default; 8192 tokens split over the "
+                         "ranks), cfg4-weak (8192 tokens per rank) or cfg5")
     ap.add_argument("--case", default="layer",
-                    help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing | hbm-write")
+                    help="layer (default) | gmm-fwd | gmm-dgrad | gmm-wgrad | routing | ops | hbm-write")
     ap.add_argument("--experts", type=int, default=None,
                     help="gmm-* cases: experts (cfg4 shapes, default 64); layer case: run a "
                          "slice of the config with this many experts (profiling)")
@@ -545,12 +789,13 @@ def main():
     ap.add_argument("--rows-per-expert", type=int, default=256, help="gmm-* cases: mean rows")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--ep-transport", choices=["auto", "nccl", "nvlink"], default="auto",
-                    help="N > 1: dispatch / combine as NCCL all-to-alls, or over NVLink peer "
-                         "memory; auto = nvlink up to 4 ranks, nccl above")
+                    help="N > 1: dispatch / combine over NVLink peer memory (auto) or as NCCL "
+                         "all-to-alls")
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-ops", action="store_true", help="N = 1: leave out the per-op block")
     ap.add_argument("--cpu-sample-experts", type=int, default=8,
                     help="experts in the CPU baseline's sample (256 rows each)")
     args = ap.parse_args()

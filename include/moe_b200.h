@@ -48,6 +48,10 @@ const char* moe_last_error_string(void);
  * kernel gave up; 2 = an expert index outside [0, E) was seen by permute. */
 int moe_read_device_error(int* code_out);
 
+/* Copies the device-side error word (4 bytes, not cleared) into `dst` (device or pinned host
+ * memory) on `stream`, without synchronising: a caller can check it a step later. */
+int moe_peek_device_error(void* dst, void* stream);
+
 /* Failure-detection self-test (no counterpart in the reference): a kernel waits on an
  * mbarrier nothing arrives at, with the bounded wait every GEMM pipeline wait uses.  After
  * timeout_ns it gives up, writes 0 to *result (device int32), records device error 1 and
@@ -159,6 +163,20 @@ int moe_gmm_dgrad(const void* grad_C, const void* B, void* grad_A, const int32_t
                   int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
                   int32_t num_experts, int trans_b, int dtype, void* stream);
 
+/* grad_A = grad_C1 . op(B1[e]) + grad_C2 . op(B2[e]) per expert row range in ONE launch: the
+ * two contractions run as consecutive segments into one fp32 accumulator, rounded once.
+ * grad_C1 [m_total, n1], grad_C2 [m_total, n2], B1 / B2 laid out as moe_gmm_dgrad's B
+ * (n1 / n2 in place of n), grad_A [m_total, k].  This is the input gradient of the gate and
+ * up projections of a SwiGLU MLP (dgrad(dgate, W_gate) + dgrad(dup, W_up)), which the
+ * reference forms with two grouped GEMMs and an add (its layer's autograd through
+ * triton_gmm_ops/grouped_gemm_ops_sm90.py:224-233 twice).  Tensor-core path only: 16-bit
+ * operands, 16-byte aligned pointers, n1, n2, k multiples of 8; MOE_ERR_INVALID_ARG
+ * otherwise (call moe_gmm_dgrad twice and add). */
+int moe_gmm_dgrad_dual(const void* grad_C1, const void* B1, const void* grad_C2, const void* B2,
+                       void* grad_A, const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                       int64_t n1, int64_t n2, int64_t k, int32_t num_experts, int trans_b,
+                       int dtype, void* stream);
+
 /* wgrad of moe_gmm_fwd: replaces tg::gmm_bwd_B_raw (grouped_gemm_ops.py:174-192).
  * grad_B [E, N, K] if trans_b else [E, K, N] (the reference supports trans_b only);
  * experts with no rows get zeros. */
@@ -216,21 +234,24 @@ int moe_ep_slot_map(const int32_t* indices, const int32_t* row_id_map, const int
                     int32_t experts_per_rank, int32_t world, int64_t capacity, int32_t* ranks,
                     int32_t* rows, void* stream);
 /* Dispatch: input row t to bases[ranks[j]] row rows[j] for each of its K slots (the
- * permute copy with peer destinations). */
+ * permute copy with peer destinations).  `status` (device int32, nullable) is the barrier
+ * status of moe_ep_barrier: when it reads 0 the kernel stores nothing (a peer that missed a
+ * barrier may still be reading its buffers).  The same holds for the two combines below,
+ * which then read no peer row (those slots contribute zero). */
 int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int32_t* ranks,
                     const int32_t* rows, int64_t num_tokens, int32_t topk, int64_t num_cols,
-                    void* stream);
+                    const int32_t* status, void* stream);
 /* Combine: out[t] = sum_k prob[t,k] * row(slot k of t) read from bases[ranks[j]], with the
  * rounding of moe_unpermute_fwd; prob NULL means 1 (the dispatch's backward). */
 int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, const int32_t* rows,
                    const void* prob, int prob_dtype, int64_t num_tokens, int32_t topk,
-                   int64_t num_cols, void* out, void* stream);
+                   int64_t num_cols, void* out, const int32_t* status, void* stream);
 /* Combine backward (moe_unpermute_bwd over peer rows): act row of slot j (in act_bases) =
  * grad_out[t] * prob[t,k]; prob_grad[t,k] = <grad_out[t], row of slot j in in_bases>. */
 int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* const* act_bases,
                        int dtype, const int32_t* ranks, const int32_t* rows, const void* prob,
                        int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols,
-                       void* prob_grad, void* stream);
+                       void* prob_grad, const int32_t* status, void* stream);
 /* dst[r] += src[r] (fp32 sum rounded to dtype) for rows r < min(*n_rows, max_rows) of two
  * [max_rows, num_cols] buffers; n_rows is a device int32 (e.g. the last grouped-GEMM
  * offset), so worst-case-sized buffers cost only their live rows. */

@@ -29,6 +29,7 @@ SIGNATURES = {
     "moe_version": (ctypes.c_char_p, []),
     "moe_last_error_string": (ctypes.c_char_p, []),
     "moe_read_device_error": (_c_int, [ctypes.POINTER(_c_int)]),
+    "moe_peek_device_error": (_c_int, [_c_ptr, _c_ptr]),
     "moe_selftest_bounded_wait": (_c_int, [ctypes.c_uint64, _c_ptr, _c_ptr]),
     "moe_write_probe": (_c_int, [_c_ptr, ctypes.c_size_t, _c_ptr]),
     "moe_ipc_malloc": (_c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _c_ptr]),
@@ -38,11 +39,11 @@ SIGNATURES = {
     "moe_ep_slot_map": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32,
                                  _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "moe_ep_dispatch": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i32, _c_i64,
-                                 _c_ptr]),
+                                 _c_ptr, _c_ptr]),
     "moe_ep_combine": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_int, _c_i64, _c_i32,
-                                _c_i64, _c_ptr, _c_ptr]),
+                                _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "moe_ep_combine_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_int,
-                                    _c_i64, _c_i32, _c_i64, _c_ptr, _c_ptr]),
+                                    _c_i64, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "moe_add_rows": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_int, _c_ptr]),
     "moe_ep_barrier": (_c_int, [_c_ptr, _c_i32, _c_i32, _c_i64, ctypes.c_uint64, _c_ptr, _c_ptr]),
     "moe_topk_softmax_fwd": (_c_int, [_c_ptr, _c_int, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr]),
@@ -69,6 +70,8 @@ SIGNATURES = {
                                           _c_ptr]),
     "moe_gmm_dgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
                                _c_int, _c_int, _c_ptr]),
+    "moe_gmm_dgrad_dual": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64,
+                                    _c_i64, _c_i64, _c_i64, _c_i32, _c_int, _c_int, _c_ptr]),
     "moe_gmm_wgrad": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
                                _c_int, _c_int, _c_ptr]),
 }

@@ -78,13 +78,6 @@ constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 16-bit columns (swizzled 16-B chunks)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
-#ifndef MOE_GMM_EPI_EXPERIMENT
-// Timing probes (results are wrong when nonzero): 1 no masked global stores, 2 no epilogue
-// work, 3 no TMA stores, 4 no staging and no TMA stores, 5 no wait for the previous TMA
-// store's read of the staging buffer, 6 16-byte global stores in place of every TMA store.
-#define MOE_GMM_EPI_EXPERIMENT 0
-#endif
-
 template <int CG>
 struct Shape {
   static constexpr int STAGES = CG == 1 ? 4 : 6;
@@ -136,6 +129,10 @@ struct Params {
                          // kModeSwiGLUBwd: grad of up (`out` holds the grad of gate)
   const void* in_gate;   // kModeSwiGLUBwd: the forward's gate [m_total, n_out]
   const void* in_up;     // kModeSwiGLUBwd: the forward's up [m_total, n_out]
+  int q_fastest;         // kModeWgrad: walk an expert's tiles output-column block fastest
+  int k_red2;            // kModeRows: > 0 adds a second contraction segment into the same
+                         // accumulator: C = A . op(B[g]) + A2 . op(B2[g]), A2 [m_total,
+                         // k_red2] through map_c2 and B2 through map_b2 (two-segment dgrad)
 };
 
 struct TileInfo {
@@ -185,11 +182,19 @@ __device__ __forceinline__ TileInfo decode_tile(const int* tile_prefix, const Pa
     ti.n_blk = local / mt;
     ti.row0 = start + ti.m_blk * TM;
     ti.rows = min(TM, rows - ti.m_blk * TM);
-    ti.nkb = (p.k_red + BK - 1) / BK;
+    ti.nkb = (p.k_red + BK - 1) / BK + (p.k_red2 + BK - 1) / BK;
   } else {
-    const int pt = (p.p_out + TM - 1) / TM;
-    ti.m_blk = local % pt;
-    ti.n_blk = local / pt;
+    if (p.q_fastest) {
+      // Concurrent tiles cover whole output rows: each row of the gradient is written in
+      // one burst of adjacent column blocks instead of one block at a time.
+      const int nt = (p.n_out + BN - 1) / BN;
+      ti.n_blk = local % nt;
+      ti.m_blk = local / nt;
+    } else {
+      const int pt = (p.p_out + TM - 1) / TM;
+      ti.m_blk = local % pt;
+      ti.n_blk = local / pt;
+    }
     ti.row0 = start;
     ti.rows = rows;
     ti.nkb = (rows + BK - 1) / BK;
@@ -329,6 +334,10 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
       ptx::prefetch_tensormap(&map_c2);
       ptx::prefetch_tensormap(&map_c3);
     }
+    if (MODE == kModeRows && p.k_red2 > 0) {
+      ptx::prefetch_tensormap(&map_b2);
+      ptx::prefetch_tensormap(&map_c2);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc<CG>(ptx::smem_u32(&s.tmem_base), kTmemCols);
@@ -402,13 +411,19 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             if (leader)
               ptx::mbar_arrive_expect_tx(
                   full_local, CG * (half ? Sh::STAGE_BYTES - Sh::A_BYTES / 2 : Sh::STAGE_BYTES));
-            const int k0 = kb * BK;
+            // Two-segment row tiles: the k-blocks past the first segment's come from the
+            // second operand pair (A2 through map_c2, B2 through map_b2).
+            const int nkb1 = (p.k_red + BK - 1) / BK;
+            const bool seg2 = MODE == kModeRows && kb >= nkb1;
+            const int k0 = (seg2 ? kb - nkb1 : kb) * BK;
+            const CUtensorMap* mapA = seg2 ? &map_c2 : &map_a;
+            const CUtensorMap* mapB = seg2 ? &map_b2 : &map_b;
             const int nb = ti.n_blk * tile_out_cols<MODE>() + (int)rank * Sh::B_COLS;
             const int a_rows = half ? BMC / 2 : BMC;
             for (int j = 0; j < a_rows / 64; ++j) {
               const int ar = ti.row0 + (int)rank * a_rows + j * 64;
-              if (CG == 1) ptx::tma_load_2d(sa + j * (64 * 128), &map_a, full_c, k0, ar);
-              else ptx::tma_load_2d_pair(sa + j * (64 * 128), &map_a, full_c, k0, ar);
+              if (CG == 1) ptx::tma_load_2d(sa + j * (64 * 128), mapA, full_c, k0, ar);
+              else ptx::tma_load_2d_pair(sa + j * (64 * 128), mapA, full_c, k0, ar);
             }
             if (MODE == kModeGateUp) {
               // B rows 0-127: gate columns nb.., rows 128-255: the same up columns.
@@ -423,13 +438,13 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 }
               }
             } else if (!B_MN) {
-              if (CG == 1) ptx::tma_load_3d(sb, &map_b, full_c, k0, nb, ti.g);
-              else ptx::tma_load_3d_pair(sb, &map_b, full_c, k0, nb, ti.g);
+              if (CG == 1) ptx::tma_load_3d(sb, mapB, full_c, k0, nb, ti.g);
+              else ptx::tma_load_3d_pair(sb, mapB, full_c, k0, nb, ti.g);
             } else {
 #pragma unroll
               for (int j = 0; j < Sh::B_COLS / 64; ++j) {
-                if (CG == 1) ptx::tma_load_3d(sb + j * (BK * 128), &map_b, full_c, nb + j * 64, k0, ti.g);
-                else ptx::tma_load_3d_pair(sb + j * (BK * 128), &map_b, full_c, nb + j * 64, k0, ti.g);
+                if (CG == 1) ptx::tma_load_3d(sb + j * (BK * 128), mapB, full_c, nb + j * 64, k0, ti.g);
+                else ptx::tma_load_3d_pair(sb + j * (BK * 128), mapB, full_c, nb + j * 64, k0, ti.g);
               }
             }
           } else {
@@ -739,15 +754,10 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         // TMA stores clip at the output's edges, so they serve every wgrad tile and every
         // warp whose 32 rows all belong to the expert; the others store with masks so they
         // never touch the next expert's rows.  A warp with no valid row stores nothing.
-        const bool use_tma = MOE_GMM_EPI_EXPERIMENT != 6 &&
-                             (MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows);
-  #if MOE_GMM_EPI_EXPERIMENT == 2
-        const int nchunks = 0;
-  #else
+        const bool use_tma = MODE == kModeWgrad || (rq + 1) * 32 <= valid_rows;
         const int nchunks = (MODE == kModeRows && valid_rows <= rq * 32)
                                 ? 0
                                 : max(0, min(ncols, valid_cols - col_lo) + 31) / 32;
-  #endif
         const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN + tcol;
         uint32_t v[32];
         const bool has_acc = ti.nkb > 0;
@@ -758,35 +768,29 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         for (int c = 0; c < nchunks; ++c) {
           uint32_t w[16];
           if (has_acc) {
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 4; ++i) {
               const uint4 u = pack8_16b<OutT>(&v[i * 8]);
               w[i * 4 + 0] = u.x; w[i * 4 + 1] = u.y; w[i * 4 + 2] = u.z; w[i * 4 + 3] = u.w;
             }
             if (c + 1 < nchunks) ptx::tmem_ld_32x32b_x32(tbase + (c + 1) * 32, v);
           } else {
-  #pragma unroll
+#pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = 0u;
           }
           // The previous TMA store from this buffer must have finished reading it.
-  #if MOE_GMM_EPI_EXPERIMENT != 5
           if (lane == 0) ptx::bulk_wait_group_read<0>();
-  #endif
           __syncwarp();
-  #if MOE_GMM_EPI_EXPERIMENT != 4
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int phys = i ^ ((wr_row >> 1) & 3);
             *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
                 make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
           }
-  #else
-          if (w[0] == 0x7fc00001u && w[15] == 0x7fc00001u) *reinterpret_cast<uint4*>(cbuf) = make_uint4(w[1], w[2], w[3], w[4]);
-  #endif
           if (use_tma) {
             ptx::fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0 && MOE_GMM_EPI_EXPERIMENT != 3 && MOE_GMM_EPI_EXPERIMENT != 4) {
+            if (lane == 0) {
               const int cx = n0 + col_lo + c * 32;
               if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
               else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
@@ -797,18 +801,14 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           }
           __syncwarp();
           const int col = col_lo + c * 32 + rd_chunk * 8;  // first column of this lane's chunk
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int rr = rd_row0 + i * 8;
             const int phys = rd_chunk ^ ((rr >> 1) & 3);
             const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
             const int row = rq * 32 + rr;
-  #if MOE_GMM_EPI_EXPERIMENT == 0 || MOE_GMM_EPI_EXPERIMENT == 6
             if (row < valid_rows && col < valid_cols)
               *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;
-  #else
-            if (u.x == 0x7fc00001u && row < 0 && col < 0) *reinterpret_cast<uint4*>(tile_ptr) = u;
-  #endif
           }
           __syncwarp();
           if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();

@@ -188,9 +188,18 @@ static int swiglu_bwd_launch(const void* grad_out, const void* gate, const void*
 // Row mode (forward / dgrad): C[m_total, n_out] = A[m_total, k_red] . op(B[g]).
 // b_mn: B[g] stored [k_red, n_out] (MN-major) instead of [n_out, k_red].
 // sw: also apply the SwiGLU backward to the product (C becomes the gate gradient).
+// seg2: a second contraction segment into the same accumulator, C = A . op(B[g]) +
+// seg2->A . op(seg2->B[g]) (tensor-core path only; the caller checks gmm_rows_dual_ok).
+struct RowsSeg2 {
+  const void* A;
+  const void* B;
+  int64_t k_red;
+};
+
 static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offsets, int plus_one,
                     int64_t m_total, int64_t n_out, int64_t k_red, int E, bool b_mn, int dtype,
-                    cudaStream_t stream, const SwiGLUBwdArgs* sw = nullptr) {
+                    cudaStream_t stream, const SwiGLUBwdArgs* sw = nullptr,
+                    const RowsSeg2* seg2 = nullptr) {
   if (m_total == 0 || n_out == 0) return MOE_OK;
   const bool tc = dtype != MOE_F32 && k_red % 8 == 0 && n_out % 8 == 0 && E <= gmm::kMaxGroups &&
                   aligned16(A) && aligned16(B) && aligned16(C) && m_total < (1ll << 31) &&
@@ -230,7 +239,7 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   }
   // Single-CTA tiles: measured on B200 against SM pairs (with half tail tiles) for 256 to
   // 2048 rows per expert at d=4096 / H=11008 shapes, they run 3-15 % faster in this mode.
-  const int cg = sw ? 1 : pick_cg(1);
+  const int cg = (sw || seg2) ? 1 : pick_cg(1);
   const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
@@ -249,6 +258,23 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     const uint64_t dims[3] = {(uint64_t)n_out, (uint64_t)k_red, (uint64_t)E};
     const uint32_t box[3] = {64, (uint32_t)gmm::BK, 1};
     int rc = make_map(&mb, B, dtype, 3, dims, box);
+    if (rc) return rc;
+  }
+  CUtensorMap ma2, mb2;  // second segment: A2 [m_total, k_red2], B2 like B
+  if (seg2) {
+    const uint64_t dims[2] = {(uint64_t)seg2->k_red, (uint64_t)m_total};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, 64u};
+    int rc = make_map(&ma2, seg2->A, dtype, 2, dims, box);
+    if (rc) return rc;
+    if (!b_mn) {
+      const uint64_t d3[3] = {(uint64_t)seg2->k_red, (uint64_t)n_out, (uint64_t)E};
+      const uint32_t b3[3] = {(uint32_t)gmm::BK, b_cols, 1};
+      rc = make_map(&mb2, seg2->B, dtype, 3, d3, b3);
+    } else {
+      const uint64_t d3[3] = {(uint64_t)n_out, (uint64_t)seg2->k_red, (uint64_t)E};
+      const uint32_t b3[3] = {64, (uint32_t)gmm::BK, 1};
+      rc = make_map(&mb2, seg2->B, dtype, 3, d3, b3);
+    }
     if (rc) return rc;
   }
   CUtensorMap mc, mc_up;  // outputs, 32 x 32 boxes in the epilogue's 64-byte swizzle
@@ -280,6 +306,16 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
                   : launch_sm100<M3, 1, 1, false, false, __nv_bfloat16>(ma, mb, mc, p, stream, extra);
     return b_mn ? launch_sm100<M3, 1, 0, false, true, __half>(ma, mb, mc, p, stream, extra)
                 : launch_sm100<M3, 1, 0, false, false, __half>(ma, mb, mc, p, stream, extra);
+  }
+  if (seg2) {
+    // map_b2 carries B2 and map_c2 carries A2 (row mode stores through map_c only).
+    p.k_red2 = (int)seg2->k_red;
+    const CUtensorMap extra[3] = {mb2, ma2, mc};
+    if (dtype == MOE_BF16)
+      return b_mn ? launch_sm100<gmm::kModeRows, 1, 1, false, true, __nv_bfloat16>(ma, mb, mc, p, stream, extra)
+                  : launch_sm100<gmm::kModeRows, 1, 1, false, false, __nv_bfloat16>(ma, mb, mc, p, stream, extra);
+    return b_mn ? launch_sm100<gmm::kModeRows, 1, 0, false, true, __half>(ma, mb, mc, p, stream, extra)
+                : launch_sm100<gmm::kModeRows, 1, 0, false, false, __half>(ma, mb, mc, p, stream, extra);
   }
   return b_mn ? launch_fmt_cg<gmm::kModeRows, false, true>(dtype, cg, ma, mb, mc, p, stream)
               : launch_fmt_cg<gmm::kModeRows, false, false>(dtype, cg, ma, mb, mc, p, stream);
@@ -343,6 +379,10 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
   p.p_out = (int)P;
   p.k_red = 0;
   p.out = Out;
+  {
+    const char* e = getenv("MOE_B200_WGRAD_ORDER");  // tuning: p = row blocks fastest
+    p.q_fastest = (e && e[0] == 'p') ? 0 : 1;
+  }
   return launch_fmt_cg<gmm::kModeWgrad, true, true>(dtype, cg, mx, my, mo, p, stream);
 }
 
@@ -415,6 +455,13 @@ int moe_read_device_error(int* code_out) {
   MOE_CUDA_CHECK(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)));
   MOE_CUDA_CHECK(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)));
   if (code_out) *code_out = v;
+  return MOE_OK;
+}
+
+int moe_peek_device_error(void* dst, void* stream) {
+  MOE_REQUIRE(dst != nullptr, "peek_device_error: dst is NULL");
+  MOE_CUDA_CHECK(cudaMemcpyFromSymbolAsync(dst, g_device_error, sizeof(int), 0, cudaMemcpyDefault,
+                                           (cudaStream_t)stream));
   return MOE_OK;
 }
 
@@ -685,6 +732,26 @@ int moe_gmm_dgrad(const void* grad_C, const void* B, void* grad_A, const int32_t
                   dtype, (cudaStream_t)stream);
 }
 
+int moe_gmm_dgrad_dual(const void* grad_C1, const void* B1, const void* grad_C2, const void* B2,
+                       void* grad_A, const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                       int64_t n1, int64_t n2, int64_t k, int32_t E, int trans_b, int dtype,
+                       void* stream) {
+  int rc = check_gmm_args(grad_C1, B1, grad_A, offsets, num_offsets, m_total, n1, k, E, dtype);
+  if (rc) return rc;
+  rc = check_gmm_args(grad_C2, B2, grad_A, offsets, num_offsets, m_total, n2, k, E, dtype);
+  if (rc) return rc;
+  if (E == 0 || m_total == 0 || k == 0) return MOE_OK;
+  MOE_REQUIRE(dtype != MOE_F32 && n1 > 0 && n2 > 0 && n1 % 8 == 0 && n2 % 8 == 0 && k % 8 == 0 &&
+                  E <= gmm::kMaxGroups && aligned16(grad_C1) && aligned16(grad_C2) &&
+                  aligned16(B1) && aligned16(B2) && aligned16(grad_A) && m_total < (1ll << 31) &&
+                  n1 < (1ll << 31) && n2 < (1ll << 31) && k < (1ll << 31),
+              "gmm_dgrad_dual: needs 16-bit operands, 16-byte aligned, n1, n2 and k multiples "
+              "of 8 (the tensor-core path); otherwise call moe_gmm_dgrad twice");
+  const RowsSeg2 seg2{grad_C2, B2, n2};
+  return gmm_rows(grad_C1, B1, grad_A, offsets, num_offsets == E + 1, m_total, k, n1, E,
+                  trans_b != 0, dtype, (cudaStream_t)stream, nullptr, &seg2);
+}
+
 int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t* offsets,
                   int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t E,
                   int trans_b, int dtype, void* stream) {
@@ -816,7 +883,10 @@ __global__ void bounded_wait_selftest_kernel(uint64_t timeout_ns, int* result) {
 // expert counts that moe_permute keeps in caller-provided workspace live instead in this
 // file-scope array, which every GPU that loads the library holds until the process exits.
 static constexpr size_t kNoAllocScratchInts = 262144;  // 1 MiB: num_tiles * E counts
-static __device__ __align__(256) int32_t g_permute_scratch[kNoAllocScratchInts];
+// moe_permute asks for 16 bytes of workspace beyond the counts, so the array carries them
+// too: a request of exactly kNoAllocScratchInts counts must still be accepted.
+static constexpr size_t kNoAllocPadInts = 4;
+static __device__ __align__(256) int32_t g_permute_scratch[kNoAllocScratchInts + kNoAllocPadInts];
 static int32_t* g_permute_scratch_ptr[64] = {nullptr};  // device address, per device
 
 size_t moe_permute_noalloc_max_slots(int32_t E) {
@@ -850,7 +920,7 @@ int moe_permute_noalloc(const void* input, int dtype, const int32_t* indices, in
   // so the array needs no clearing; calls that overlap on the GPU share it and race.
   return moe_permute(input, dtype, indices, num_tokens, topk, num_cols, E, num_out, permuted,
                      row_id_map, offsets, g_permute_scratch_ptr[dev],
-                     kNoAllocScratchInts * sizeof(int32_t), stream);
+                     (kNoAllocScratchInts + kNoAllocPadInts) * sizeof(int32_t), stream);
 }
 
 // ---------------------------------------------------------------- expert parallelism over peer memory
@@ -904,7 +974,7 @@ int moe_ep_slot_map(const int32_t* indices, const int32_t* row_id_map, const int
 
 int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int32_t* ranks,
                     const int32_t* rows, int64_t num_tokens, int32_t topk, int64_t num_cols,
-                    void* stream) {
+                    const int32_t* status, void* stream) {
   MOE_REQUIRE(dtype_ok(dtype), "ep_dispatch: bad dtype %d", dtype);
   MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_dispatch: bad sizes");
   MOE_REQUIRE(aligned16(input), "ep_dispatch: input must be 16-byte aligned");
@@ -916,7 +986,7 @@ int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int3
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
 #define MOE_EPD(TT)                                                                                  \
   {                                                                                                 \
-    const PeerRows<TT> r{(TT* const*)bases, ranks, rows, num_tokens, num_cols};                      \
+    const PeerRows<TT> r{(TT* const*)bases, ranks, rows, num_tokens, num_cols, status};              \
     if (vec)                                                                                        \
       permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, r,             \
                                                                     num_tokens, topk, num_cols);   \
@@ -936,7 +1006,7 @@ int moe_ep_dispatch(const void* input, int dtype, void* const* bases, const int3
 
 int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, const int32_t* rows,
                    const void* prob, int prob_dtype, int64_t num_tokens, int32_t topk,
-                   int64_t num_cols, void* out, void* stream) {
+                   int64_t num_cols, void* out, const int32_t* status, void* stream) {
   MOE_REQUIRE(dtype_ok(dtype) && (prob == nullptr || dtype_ok(prob_dtype)),
               "ep_combine: bad dtype %d / prob dtype %d", dtype, prob_dtype);
   MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_combine: bad sizes");
@@ -948,7 +1018,7 @@ int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, co
   const int pd = prob == nullptr ? MOE_F32 : prob_dtype;
 #define MOE_EPC(TT, PP)                                                                              \
   {                                                                                                 \
-    const PeerRows<const TT> r{(const TT* const*)bases, ranks, rows, num_tokens, num_cols};          \
+    const PeerRows<const TT> r{(const TT* const*)bases, ranks, rows, num_tokens, num_cols, status};  \
     if (vec)                                                                                        \
       unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                            \
           r, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
@@ -976,7 +1046,7 @@ int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, co
 int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* const* act_bases,
                        int dtype, const int32_t* ranks, const int32_t* rows, const void* prob,
                        int prob_dtype, int64_t num_tokens, int32_t topk, int64_t num_cols,
-                       void* prob_grad, void* stream) {
+                       void* prob_grad, const int32_t* status, void* stream) {
   MOE_REQUIRE(dtype_ok(dtype) && dtype_ok(prob_dtype), "ep_combine_bwd: bad dtype");
   MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0, "ep_combine_bwd: bad sizes");
   MOE_REQUIRE(prob != nullptr && prob_grad != nullptr, "ep_combine_bwd: prob / prob_grad is NULL");
@@ -987,8 +1057,9 @@ int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* 
   const dim3 grid((unsigned)((num_tokens + kRowWarps - 1) / kRowWarps));
 #define MOE_EPB(TT, PP, KM)                                                                          \
   {                                                                                                 \
-    const PeerRows<const TT> ir{(const TT* const*)in_bases, ranks, rows, num_tokens, num_cols};     \
-    const PeerRows<TT> ar{(TT* const*)act_bases, ranks, rows, num_tokens, num_cols};                \
+    const PeerRows<const TT> ir{(const TT* const*)in_bases, ranks, rows, num_tokens, num_cols,      \
+                                status};                                                            \
+    const PeerRows<TT> ar{(TT* const*)act_bases, ranks, rows, num_tokens, num_cols, status};        \
     if (vec)                                                                                        \
       unpermute_bwd_kernel<TT, PP, KM, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
           (const TT*)grad_out, ir, ar, (const PP*)prob, (PP*)prob_grad, num_tokens, topk, num_cols);\

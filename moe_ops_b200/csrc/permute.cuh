@@ -176,6 +176,9 @@ constexpr int kRowWarps = 8;  // warps (tokens) per block for the row kernels
 //   LocalRows: one buffer, rows from row_id_map (k-major [K*T], -1 = no row).
 //   PeerRows:  rows spread over the ranks' buffers (expert parallelism over peer memory):
 //              slot j = k*T + t lives in bases[ranks[j]] at row rows[j]; ranks[j] < 0 = none.
+//              When `status` is given and reads 0 (a cross-GPU barrier of this step gave
+//              up), every slot reads as none: the kernel touches no peer buffer, because
+//              the peers may still be using them.
 template <typename T>
 struct LocalRows {
   static constexpr bool kPeer = false;
@@ -196,7 +199,9 @@ struct PeerRows {
   const int32_t* ranks;
   const int32_t* rows;
   int64_t num_tokens, num_cols;
+  const int32_t* status;  // nullable
   __device__ __forceinline__ int32_t row(int k, int64_t t) const {
+    if (status != nullptr && *status == 0) return -1;
     const int64_t j = (int64_t)k * num_tokens + t;
     return ranks[j] < 0 ? -1 : rows[j];
   }

@@ -127,7 +127,8 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
                    w_up_local: torch.Tensor, w_down_local: torch.Tensor, top_k: int,
                    num_experts: int, ops: EPOps | None = None, group=None,
                    fp32_routing: bool = False,
-                   router_bias: torch.Tensor | None = None) -> torch.Tensor:
+                   router_bias: torch.Tensor | None = None,
+                   stats: dict | None = None) -> torch.Tensor:
     """One expert-parallel SwiGLU MoE layer on this rank's tokens x [T, d].
 
     w_router [E, d] is replicated; w_*_local hold this rank's E/W experts
@@ -147,6 +148,8 @@ def ep_moe_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate_local: torch.
     counts = send_counts(offsets, world)
     recv_counts, send_sizes, recv_sizes = exchange_counts(counts, world, group)
     n_recv = sum(recv_sizes)
+    if stats is not None:
+        stats["local_rows"] = n_recv
     recv = all_to_all_rows(permuted[: T * top_k], send_sizes, recv_sizes, group)
     ids = local_expert_ids(recv_counts, world, n_recv)
     grouped, rid2, off2 = ops.permute(recv, ids.unsqueeze(1), el)
@@ -189,17 +192,40 @@ class EPMoELayer(torch.nn.Module):
         # The peer path needs the same token count on every rank.
         self.transport = "nccl"
         self._peer = None
+        self._peer_tokens = 0
+        # Largest token count any rank passes (sizes the peer buffers); None: the largest T
+        # of the first call, agreed on by all ranks.
+        self.max_tokens = None
+        self._last_local_rows = 0
 
     def _forward_peer(self, x):
         from .ep_peer import NVLinkTransport, capacity_rows, peer_experts
         from .fused_topk_softmax_ops import fused_topk_softmax
 
         world = dist.get_world_size(self.group)
-        cap = capacity_rows(x.shape[0], self.top_k, world)
-        if self._peer is None or self._peer.capacity < cap or self._peer.cols != x.shape[1]:
-            if self._peer is not None:
-                self._peer.close()
-            self._peer = NVLinkTransport(self.group, cap, x.shape[1], x.dtype, x.device)
+        T = x.shape[0]
+        if self._peer is None:
+            # Collective on every rank: the buffers are sized for the largest token count of
+            # any rank (max_tokens if set, else the largest T of this first call), so a slot
+            # can never land past the end of a peer's receive buffer, whatever the ranks'
+            # token counts are later (each at most that size).
+            if self.max_tokens is not None:
+                t_max = int(self.max_tokens)
+            else:
+                t = torch.tensor([T], dtype=torch.int64, device=x.device)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+                t_max = int(t.item())
+            self._peer = NVLinkTransport(self.group, capacity_rows(t_max, self.top_k, world),
+                                         x.shape[1], x.dtype, x.device)
+            self._peer_tokens = t_max
+        else:
+            self._peer.check_health()
+        if T > self._peer_tokens or x.shape[1] != self._peer.cols or x.dtype != self._peer.dtype:
+            # Rebuilding here would be a collective that only this rank enters.
+            raise RuntimeError(
+                f"EP peer transport was built for at most {self._peer_tokens} tokens of "
+                f"{self._peer.cols} {self._peer.dtype} columns per rank; got {tuple(x.shape)} "
+                f"{x.dtype}. Call close() on every rank (or set max_tokens) to rebuild it.")
         logits = x @ self.w_router.t()
         if self.router_bias is not None:
             logits = logits + self.router_bias
@@ -208,6 +234,17 @@ class EPMoELayer(torch.nn.Module):
         weights, indices = fused_topk_softmax(logits, self.top_k)
         return peer_experts(x, weights, indices, self.w_gate, self.w_up, self.w_down, self._peer,
                             self.num_experts)
+
+    def local_rows(self) -> int:
+        """Rows this rank's experts computed on in the last forward (synchronises): the
+        count the grouped GEMMs' FLOPs follow, whatever the buffers' capacity."""
+        if self.transport == "nvlink" and self._peer is not None:
+            return int(self._peer.last_local_rows.item())
+        return int(self._last_local_rows)
+
+    def health_ok(self) -> bool:
+        """True unless a peer-memory barrier gave up (synchronises; NCCL path: True)."""
+        return self._peer is None or self._peer.barrier_ok()
 
     def close(self):
         """Releases the peer-memory buffers (collective when they exist: every rank calls
@@ -220,13 +257,20 @@ class EPMoELayer(torch.nn.Module):
         if self.transport == "nvlink":
             return self._forward_peer(x)
         if self.chunks > 0:
-            return ep_moe_forward_overlapped(x, self.w_router, self.w_gate, self.w_up, self.w_down,
-                                             self.top_k, self.num_experts, group=self.group,
-                                             fp32_routing=self.fp32_routing,
-                                             router_bias=self.router_bias, chunks=self.chunks)
-        return ep_moe_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down, self.top_k,
-                              self.num_experts, group=self.group, fp32_routing=self.fp32_routing,
-                              router_bias=self.router_bias)
+            stats = {}
+            out = ep_moe_forward_overlapped(x, self.w_router, self.w_gate, self.w_up, self.w_down,
+                                            self.top_k, self.num_experts, group=self.group,
+                                            fp32_routing=self.fp32_routing,
+                                            router_bias=self.router_bias, chunks=self.chunks,
+                                            stats=stats)
+            self._last_local_rows = stats["local_rows"]
+            return out
+        stats = {}
+        out = ep_moe_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down, self.top_k,
+                             self.num_experts, group=self.group, fp32_routing=self.fp32_routing,
+                             router_bias=self.router_bias, stats=stats)
+        self._last_local_rows = stats["local_rows"]
+        return out
 
 
 # ------------------------------------------------------------------ overlapped expert segment
@@ -316,8 +360,8 @@ class _OverlappedExperts(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_home):
-        from .gate_up_ops import gmm_dgrad_swiglu_bwd_raw
-        from .grouped_gemm_ops import _gmm_call, gmm_dgrad_raw
+        from .gate_up_ops import gmm_dgrad_dual_raw, gmm_dgrad_swiglu_bwd_raw
+        from .grouped_gemm_ops import _gmm_call
         from .permute_ops import permute_backward
 
         w_gate, w_up, w_down = ctx.saved_tensors
@@ -348,8 +392,7 @@ class _OverlappedExperts(torch.autograd.Function):
             dgate, dup = gmm_dgrad_swiglu_bwd_raw(g_down_rows, w_down[e0:e1], gate, up, off2, True)
             _gmm_call("moe_gmm_wgrad", h, g_down_rows, g_down[e0:e1], off2, n, w_down.shape[1],
                       w_down.shape[2], el, True)
-            dgrouped = gmm_dgrad_raw(dgate, w_gate[e0:e1], off2, True)
-            dgrouped += gmm_dgrad_raw(dup, w_up[e0:e1], off2, True)
+            dgrouped = gmm_dgrad_dual_raw(dgate, w_gate[e0:e1], dup, w_up[e0:e1], off2, True)
             _gmm_call("moe_gmm_wgrad", grouped, dgate, g_gate[e0:e1], off2, n, w_gate.shape[1],
                       w_gate.shape[2], el, True)
             _gmm_call("moe_gmm_wgrad", grouped, dup, g_up[e0:e1], off2, n, w_up.shape[1],
@@ -364,7 +407,7 @@ class _OverlappedExperts(torch.autograd.Function):
 
 def ep_moe_forward_overlapped(x, w_router, w_gate_local, w_up_local, w_down_local, top_k,
                               num_experts, group=None, fp32_routing=False, router_bias=None,
-                              chunks: int = 2):
+                              chunks: int = 2, stats: dict | None = None):
     """ep_moe_forward with the dispatch / combine all-to-alls overlapped with the expert
     GEMMs (CUDA ops only)."""
     from . import fused_topk_softmax, permute, unpermute
@@ -384,6 +427,8 @@ def ep_moe_forward_overlapped(x, w_router, w_gate_local, w_up_local, w_down_loca
     both = torch.stack([counts, recv]).cpu()
     send_cnt = both[0].reshape(world, el).tolist()
     recv_cnt = both[1].reshape(world, el).tolist()
+    if stats is not None:
+        stats["local_rows"] = sum(map(sum, recv_cnt))
     bounds = _chunk_bounds(el, chunks)
     plan = {"bounds": bounds, "chunks": _segment_plan(send_cnt, recv_cnt, bounds)}
     home = _OverlappedExperts.apply(permuted[: T * top_k], w_gate_local, w_up_local,

@@ -120,8 +120,20 @@ class NVLinkTransport(PeerTransport):
             self._flags.zero_()
             self._flag_table = torch.tensor(table[-1], dtype=torch.int64, device=self.device)
             self._status = torch.ones(1, dtype=torch.int32, device=self.device)
+            # Health of the previous steps, copied to pinned host memory at the end of every
+            # backward and read (without a sync) at the start of a later forward.
+            self._health_host = torch.zeros(2, dtype=torch.int32).pin_memory()
+            self._health_dev = torch.zeros(2, dtype=torch.int32, device=self.device)
+            self._health_event = None
             torch.cuda.synchronize(self.device)
+        self.step = 0                 # forwards run so far (a backward checks it)
+        self.pending_backward = False
         dist.barrier(group=group)  # every rank's flags are zero before the first signal
+
+    @property
+    def status(self) -> torch.Tensor:
+        """Device int32 [1]: 1 while every barrier so far completed, 0 after one gave up."""
+        return self._status
 
     def all_gather_counts(self, counts):
         out = torch.empty(self.world, counts.numel(), dtype=counts.dtype, device=counts.device)
@@ -141,11 +153,39 @@ class NVLinkTransport(PeerTransport):
         """False if any barrier so far gave up waiting (reads the status: syncs)."""
         return bool(self._status.item())
 
+    def record_health(self) -> None:
+        """Enqueues a copy of the barrier status and the library's device error word into
+        pinned host memory (no sync); check_health() reads it once it has landed."""
+        lib = _lib.load()
+        stream = torch.cuda.current_stream(self.device)
+        self._health_dev[:1].copy_(self._status)
+        _lib.check(lib.moe_peek_device_error(_lib.ptr(self._health_dev[1:]), stream.cuda_stream),
+                   "moe_peek_device_error")
+        self._health_host.copy_(self._health_dev, non_blocking=True)
+        self._health_event = torch.cuda.Event()
+        self._health_event.record(stream)
+
+    def check_health(self) -> None:
+        """Raises if an earlier step's barrier gave up or a kernel raised a device error.
+        Reads the last record_health() copy only if it has completed: never syncs."""
+        ev = self._health_event
+        if ev is None or not ev.query():
+            return
+        status, err = self._health_host.tolist()
+        if status == 0 or err != 0:
+            raise RuntimeError(
+                f"EP peer transport (rank {self.rank}): an earlier step failed (barrier "
+                f"status {status}, device error {err}); its results are not valid. Close the "
+                "layer on every rank and rebuild it.")
+
     def close(self):
         """Collective: unmaps the peers' buffers, waits until every rank has done so, then
         frees this rank's own (an exporter must not free memory a peer still maps)."""
         if not self._own:
             return
+        if self.pending_backward:
+            raise RuntimeError("NVLinkTransport.close(): a forward's backward has not run yet; "
+                               "it still needs these buffers")
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
         lib = _lib.load()
@@ -188,12 +228,17 @@ class _PeerExperts(torch.autograd.Function):
         T, d = x.shape
         K = indices.shape[1]
         E, W = num_experts, tr.world
+        status = getattr(tr, "status", None)
+        tr.step = getattr(tr, "step", 0) + 1
+        ctx.step = tr.step
+        tr.pending_backward = any(ctx.needs_input_grad)
         El = E // W
         x = x.contiguous()
         indices = indices.to(torch.int32).contiguous()
         _, rid, offsets = permute_countsort(x[:, :0], indices, 0, E)   # index pass only
         counts_all = tr.all_gather_counts(offsets[1:] - offsets[:-1])
         delta, off_local = _layout(counts_all, offsets, tr.rank, W)
+        tr.last_local_rows = off_local[El:]  # rows this rank's experts compute on (device)
         ranks = torch.empty(T * K, dtype=torch.int32, device=x.device)
         rows = torch.empty_like(ranks)
         stream = _lib.stream_of(x)
@@ -203,7 +248,8 @@ class _PeerExperts(torch.autograd.Function):
         dt = _lib.dtype_code(x.dtype)
         tr.barrier()                                               # B1
         _lib.check(lib.moe_ep_dispatch(_lib.ptr(x), dt, _lib.ptr(tr.bases["recv"]), _lib.ptr(ranks),
-                                       _lib.ptr(rows), T, K, d, stream), "moe_ep_dispatch")
+                                       _lib.ptr(rows), T, K, d, _lib.ptr(status), stream),
+                   "moe_ep_dispatch")
         tr.barrier()                                               # B2
         recv, down = tr.buffers["recv"], tr.buffers["down"]
         gate, up, h = gmm_gate_up_fwd_raw(recv, w_gate, w_up, off_local, True)
@@ -214,7 +260,7 @@ class _PeerExperts(torch.autograd.Function):
         w = weights.contiguous()
         _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["down"]), dt, _lib.ptr(ranks), _lib.ptr(rows),
                                       _lib.ptr(w), _lib.dtype_code(w.dtype), T, K, d, _lib.ptr(out),
-                                      stream), "moe_ep_combine")
+                                      _lib.ptr(status), stream), "moe_ep_combine")
         _lib.count_launches(3)
         ctx.save_for_backward(w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down)
         ctx.tr, ctx.shape = tr, (T, K, d, El)
@@ -222,11 +268,19 @@ class _PeerExperts(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        from .gate_up_ops import gmm_dgrad_swiglu_bwd_raw
+        from .gate_up_ops import dgrad_dual_into, dgrad_dual_ok, gmm_dgrad_swiglu_bwd_raw
         from .grouped_gemm_ops import _gmm_call, gmm_bwd_B_raw, gmm_dgrad_raw
 
         w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down = ctx.saved_tensors
         tr = ctx.tr
+        if getattr(tr, "step", ctx.step) != ctx.step:
+            # The transport's shared buffers (received rows, expert outputs) now hold a later
+            # forward's rows: this backward would silently mix the two steps.
+            raise RuntimeError(
+                "EP peer transport: backward of forward step %d after step %d ran; the "
+                "peer-memory layer needs each backward before the next forward" %
+                (ctx.step, tr.step))
+        status = getattr(tr, "status", None)
         T, K, d, El = ctx.shape
         lib = _lib.load()
         grad_out = grad_out.to(w_down.dtype).contiguous()
@@ -236,23 +290,32 @@ class _PeerExperts(torch.autograd.Function):
         _lib.check(lib.moe_ep_combine_bwd(_lib.ptr(grad_out), _lib.ptr(tr.bases["down"]),
                                           _lib.ptr(tr.bases["gdown"]), dt, _lib.ptr(ranks),
                                           _lib.ptr(rows), _lib.ptr(w), _lib.dtype_code(w.dtype), T, K,
-                                          d, _lib.ptr(grad_w), stream), "moe_ep_combine_bwd")
+                                          d, _lib.ptr(grad_w), _lib.ptr(status), stream),
+                   "moe_ep_combine_bwd")
         tr.barrier()                                               # B4
         recv, gdown, dgrad = tr.buffers["recv"], tr.buffers["gdown"], tr.buffers["dgrad"]
         dgate, dup = gmm_dgrad_swiglu_bwd_raw(gdown, w_down, gate, up, off_local, True)
         g_down = gmm_bwd_B_raw(h, w_down, off_local, gdown, True)
-        _gmm_call("moe_gmm_dgrad", dgate, w_gate, dgrad, off_local, tr.capacity, w_gate.shape[1],
-                  w_gate.shape[2], El, True)
-        dgrad_up = gmm_dgrad_raw(dup, w_up, off_local, True)
-        _lib.check(lib.moe_add_rows(_lib.ptr(dgrad), _lib.ptr(dgrad_up), _lib.ptr(off_local[El:]),
-                                    tr.capacity, d, dt, stream), "moe_add_rows")
+        if dgrad_dual_ok(dgate, w_gate, dup, w_up):
+            dgrad_dual_into(dgate, w_gate, dup, w_up, dgrad, off_local, tr.capacity, True)
+        else:
+            _gmm_call("moe_gmm_dgrad", dgate, w_gate, dgrad, off_local, tr.capacity,
+                      w_gate.shape[1], w_gate.shape[2], El, True)
+            dgrad_up = gmm_dgrad_raw(dup, w_up, off_local, True)
+            _lib.check(lib.moe_add_rows(_lib.ptr(dgrad), _lib.ptr(dgrad_up),
+                                        _lib.ptr(off_local[El:]), tr.capacity, d, dt, stream),
+                       "moe_add_rows")
         g_gate = gmm_bwd_B_raw(recv, w_gate, off_local, dgate, True)
         g_up = gmm_bwd_B_raw(recv, w_up, off_local, dup, True)
         tr.barrier()                                               # B5
         grad_x = torch.empty(T, d, device=grad_out.device, dtype=grad_out.dtype)
         _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["dgrad"]), dt, _lib.ptr(ranks), _lib.ptr(rows),
-                                      None, 0, T, K, d, _lib.ptr(grad_x), stream), "moe_ep_combine")
+                                      None, 0, T, K, d, _lib.ptr(grad_x), _lib.ptr(status), stream),
+                   "moe_ep_combine")
         _lib.count_launches(3)
+        tr.pending_backward = False
+        if hasattr(tr, "record_health"):
+            tr.record_health()
         return grad_x, grad_w, None, g_gate, g_up, g_down, None, None
 
 

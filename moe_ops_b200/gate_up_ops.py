@@ -11,8 +11,10 @@ The reference's example layer runs two grouped GEMMs and a PyTorch SwiGLU
 ``grouped_gemm_swiglu(permuted, w_gate, w_up, offsets)`` returns the same ``h`` from one
 tensor-core launch: each tile accumulates 128 gate and 128 up columns of the same rows, and
 its epilogue writes gate, up (kept for the backward) and h.  The three outputs equal the
-unfused sequence bit for bit (same accumulation order, same rounding steps).  Its backward
-is the unfused one: SwiGLU backward, two dgrad GEMMs summed, two wgrad GEMMs.
+unfused sequence bit for bit (same accumulation order, same rounding steps).  Its backward:
+SwiGLU backward, the two dgrad GEMMs as one two-segment launch into one accumulator
+(``gmm_dgrad_dual_raw``: rounded once, so it differs from the unfused dgrad + dgrad + add by
+at most the add's rounding), two wgrad GEMMs.
 
 ``grouped_swiglu_mlp(permuted, w_gate, w_up, w_down, offsets)`` is the whole expert MLP,
 ``grouped_gemm(h, w_down)`` on top of the above.  Its backward runs the down projection's
@@ -121,11 +123,73 @@ def _(grad_output, B, gate, up, offsets, trans_b=True):
     return torch.empty_like(gate), torch.empty_like(up)
 
 
+def dgrad_dual_ok(g1: torch.Tensor, B1: torch.Tensor, g2: torch.Tensor, B2: torch.Tensor) -> bool:
+    """True when moe_gmm_dgrad_dual takes these operands (its tensor-core conditions)."""
+    ts = (g1, B1, g2, B2)
+    return (g1.dtype in (torch.float16, torch.bfloat16)
+            and all(t.dtype == g1.dtype and t.is_contiguous() and t.data_ptr() % 16 == 0 for t in ts)
+            and g1.shape[1] % 8 == 0 and g2.shape[1] % 8 == 0 and B1.shape[0] <= 1024
+            and B1.shape[1] % 8 == 0 and B1.shape[2] % 8 == 0)
+
+
+def dgrad_dual_into(g1, B1, g2, B2, out, offsets, m_total: int, trans_b: bool) -> None:
+    """out[:m_total] = g1 . op(B1[e]) + g2 . op(B2[e]) per expert row range, in one
+    tensor-core launch (moe_gmm_dgrad_dual); the operands must pass dgrad_dual_ok."""
+    _lib.require_cuda(g1, B1, g2, B2, out, offsets)
+    E = B1.shape[0]
+    k = B1.shape[2] if trans_b else B1.shape[1]
+    n1, n2 = g1.shape[1], g2.shape[1]
+    lib = _lib.load()
+    timing = _lib.gemm_timing
+    with torch.cuda.device(g1.device):
+        if timing is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        st = lib.moe_gmm_dgrad_dual(
+            _lib.ptr(g1), _lib.ptr(B1), _lib.ptr(g2), _lib.ptr(B2), _lib.ptr(out),
+            _lib.ptr(offsets), offsets.numel(), m_total, n1, n2, k, E, int(bool(trans_b)),
+            _lib.dtype_code(g1.dtype), _lib.stream_of(g1))
+        if timing is not None:
+            ev1.record()
+            es = g1.element_size()
+            timing.append(("moe_gmm_dgrad_dual", ev0, ev1, 2.0 * m_total * (n1 + n2) * k,
+                           E * (n1 + n2) * k * es + m_total * (n1 + n2) * es, m_total * k * es))
+    _lib.check(st, "moe_gmm_dgrad_dual")
+    _lib.count_launches(1)
+
+
+@torch.library.custom_op(f"{_NS}::gmm_dgrad_dual_raw", mutates_args=())
+def gmm_dgrad_dual_raw(grad_1: torch.Tensor, B_1: torch.Tensor, grad_2: torch.Tensor,
+                       B_2: torch.Tensor, offsets: torch.Tensor,
+                       trans_b: bool = True) -> torch.Tensor:
+    """grad_A = dgrad(grad_1, B_1) + dgrad(grad_2, B_2) with one rounding, one launch when
+    the tensor-core path takes the operands, else two dgrad launches and an add."""
+    grad_1, grad_2 = grad_1.contiguous(), grad_2.contiguous()
+    B_1, B_2 = B_1.contiguous(), B_2.contiguous()
+    E = B_1.shape[0]
+    offsets = _norm_offsets(offsets, E)
+    if not dgrad_dual_ok(grad_1, B_1, grad_2, B_2):
+        out = gmm_dgrad_raw(grad_1, B_1, offsets, trans_b)
+        out += gmm_dgrad_raw(grad_2, B_2, offsets, trans_b)
+        return out
+    k = B_1.shape[2] if trans_b else B_1.shape[1]
+    out = torch.empty((grad_1.shape[0], k), device=grad_1.device, dtype=grad_1.dtype)
+    dgrad_dual_into(grad_1, B_1, grad_2, B_2, out, offsets, grad_1.shape[0], trans_b)
+    return out
+
+
+@gmm_dgrad_dual_raw.register_fake
+def _(grad_1, B_1, grad_2, B_2, offsets, trans_b=True):
+    k = B_1.shape[2] if trans_b else B_1.shape[1]
+    return torch.empty((grad_1.shape[0], k), device=grad_1.device, dtype=grad_1.dtype)
+
+
 def _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b, needs):
     grad_A = grad_g = grad_u = None
     if needs[0]:
-        grad_A = gmm_dgrad_raw(dgate, B_gate, offsets, trans_b)
-        grad_A += gmm_dgrad_raw(dup, B_up, offsets, trans_b)
+        # dgrad of both projections into one accumulator: one launch, one rounding
+        grad_A = gmm_dgrad_dual_raw(dgate, B_gate, dup, B_up, offsets, trans_b)
     if needs[1]:
         grad_g = gmm_bwd_B_raw(A, B_gate, offsets, dgate, trans_b)
     if needs[2]:
@@ -188,4 +252,4 @@ def grouped_swiglu_mlp(A: torch.Tensor, B_gate: torch.Tensor, B_up: torch.Tensor
 
 
 __all__ = ["grouped_gemm_swiglu", "grouped_swiglu_mlp", "gmm_gate_up_fwd_raw",
-           "gmm_dgrad_swiglu_bwd_raw"]
+           "gmm_dgrad_swiglu_bwd_raw", "gmm_dgrad_dual_raw"]

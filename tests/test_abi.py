@@ -123,6 +123,8 @@ def test_every_custom_op_has_a_fake_impl():
             "gmm_bwd_B_raw": (ops.gmm_bwd_B_raw(A, Wgu, off, gate, True), [((E, H, d), bf)]),
             "gmm_gate_up_fwd_raw": (ops.gmm_gate_up_fwd_raw(A, Wgu, Wgu, off, True),
                                     [((T * K, H), bf)] * 3),
+            "gmm_dgrad_dual_raw": (ops.gmm_dgrad_dual_raw(gate, Wgu, gate, Wgu, off, True),
+                                   [((T * K, d), bf)]),
             "gmm_dgrad_swiglu_bwd_raw": (
                 ops.gmm_dgrad_swiglu_bwd_raw(A, Wd, gate, gate, off, True), [((T * K, H), bf)] * 2),
             "permute_countsort": (ops.permute_countsort(x, idx, 0, E),

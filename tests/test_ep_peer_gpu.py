@@ -81,7 +81,7 @@ class _EmulatedTransport:
         self._sh["bar"].wait()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_emulated_ranks_match_single_gpu(cuda_dev, world):
     import moe_ops_b200 as M
     from moe_ops_b200 import _lib
@@ -153,10 +153,22 @@ def test_out_of_range_destination_is_refused(cuda_dev):
     bases = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device=cuda_dev)
     x = torch.ones(T, 16, dtype=torch.bfloat16, device=cuda_dev)
     assert lib.moe_ep_dispatch(_lib.ptr(x), 2, _lib.ptr(bases), _lib.ptr(ranks), _lib.ptr(rows),
-                               T, K, 16, _lib.stream_of(x)) == 0
+                               T, K, 16, None, _lib.stream_of(x)) == 0
     written = sum(int((b != 0).any(1).sum()) for b in bufs)
     assert written == int((flat != 2).sum())
     assert _lib.read_device_error() == 3  # read and cleared
+    # After a barrier gave up (status 0) the row kernels touch no peer buffer at all.
+    for b in bufs:
+        b.zero_()
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    assert lib.moe_ep_dispatch(_lib.ptr(x), 2, _lib.ptr(bases), _lib.ptr(ranks), _lib.ptr(rows),
+                               T, K, 16, _lib.ptr(status), _lib.stream_of(x)) == 0
+    out = torch.full((T, 16), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    assert lib.moe_ep_combine(_lib.ptr(bases), 2, _lib.ptr(ranks), _lib.ptr(rows), None, 0, T, K,
+                              16, _lib.ptr(out), _lib.ptr(status), _lib.stream_of(x)) == 0
+    torch.cuda.synchronize()
+    assert sum(int((b != 0).any(1).sum()) for b in bufs) == 0
+    assert (out == 0).all()  # every slot read as absent
 
 
 def test_barrier_gives_up_on_a_silent_peer(cuda_dev):

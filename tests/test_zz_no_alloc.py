@@ -67,3 +67,20 @@ def test_noalloc_rejects_oversized_requests(cuda_dev):
     st = lib.moe_permute_noalloc(None, 2, None, T, K, 64, E, T * K, None, None, None, None)
     assert st == 1
     assert b"scratch" in ctypes.c_char_p(lib.moe_last_error_string()).value
+
+
+@pytest.mark.parametrize("E,K,C", [(256, 8, 64), (1024, 2, 64)])
+def test_noalloc_accepts_its_documented_maximum(cuda_dev, E, K, C):
+    """T*K == moe_permute_noalloc_max_slots(E) is the largest size the header promises."""
+    lib = _lib.load()
+    max_slots = lib.moe_permute_noalloc_max_slots(E)
+    assert max_slots % K == 0
+    T = max_slots // K
+    g = torch.Generator(device=cuda_dev).manual_seed(E)
+    x = torch.randn(T, C, device=cuda_dev, generator=g).to(torch.bfloat16)
+    idx = torch.randint(0, E, (T, K), device=cuda_dev, generator=g, dtype=torch.int32)
+    for _ in range(2):
+        (p0, r0, o0), (p1, r1, o1) = _permute_both(lib, x, idx, E)
+        assert torch.equal(o0, o1)
+        assert torch.equal(r0, r1)
+        assert torch.equal(p0, p1)
