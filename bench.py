@@ -179,6 +179,14 @@ class ClockSampler:
                 "reason_bits": hex(self.bits), "samples": len(self.samples)}
 
 
+def _progress(msg: str) -> None:
+    """One line on stderr per phase of a run (rank-tagged), so a run cut short shows where."""
+    if os.environ.get("MOE_BENCH_QUIET"):
+        return
+    sys.stderr.write(f"[bench rank {os.environ.get('RANK', '0')} {time.strftime('%H:%M:%S')}] {msg}\n")
+    sys.stderr.flush()
+
+
 def _make_inputs(dev, T, d, seed):
     g = torch.Generator(device=dev).manual_seed(seed)
     x = torch.randn(T, d, device=dev, generator=g).to(torch.bfloat16)
@@ -250,11 +258,13 @@ def ep_parity_check(world, rank, dev, transport, T=512, d=256, K=2, H=512, tol=1
         o = moe_layer_forward(xa.detach().cpu().float(), wr.float(), wg.float(), wu.float(),
                               wd.float(), K, E, routing=(w_.cpu().float(), idx.cpu()))
         errs["out_vs_oracle"] = rel(ref, o)
+    # Every rank contributes the same entries (a collective over tensors of different sizes
+    # would never complete): the oracle entry is rank 0's and reads 0 elsewhere.
+    errs.setdefault("out_vs_oracle", 0.0)
     names = sorted(errs)
-    t = torch.tensor([errs.get(n, 0.0) for n in names] + [0.0 if healthy else 1.0,
-                                                          float(_lib.read_device_error())],
+    t = torch.tensor([errs[n] for n in names] + [0.0 if healthy else 1.0,
+                                                 float(_lib.read_device_error())],
                      device=dev, dtype=torch.float64)
-    # rank 0 alone has the oracle entry; every rank has the others
     allt = [torch.zeros_like(t) for _ in range(world)]
     dist.all_gather(allt, t)
     mx = torch.stack(allt).max(0).values.tolist()
@@ -306,7 +316,9 @@ def run_ours(args):
         transport = args.ep_transport if args.ep_transport != "auto" else "nvlink"
         args.ep_transport = transport
         # Correctness of the multi-GPU layer, over the same transport, before timing it.
+        _progress(f"ep parity check ({transport})")
         parity = ep_parity_check(world, rank, dev, transport)
+        _progress(f"ep parity: ok={parity['ok']} max_rel_err={parity['max_rel_err']}")
         if not parity["ok"]:
             if rank == 0:
                 print(json.dumps({"metric": METRIC, "error": "ep parity check failed",
@@ -344,10 +356,12 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    _progress("warm-up")
     for _ in range(max(args.warmup, 3)):
         step(x, grad_out)
     barrier()
     torch.cuda.reset_peak_memory_stats(dev)
+    _progress("timed region")
 
     # ------------------------------------------------------------ device-timed region
     sampler = ClockSampler(local)
@@ -383,6 +397,53 @@ def run_ours(args):
         mem_s = max((t[4] + t[5]) / (peaks_["hbm_gbs"] * 1e9), t[5] / (write_gbs * 1e9))
         t_roof += max(flop_s, mem_s)
     peak_mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    eager_ms_total, eager_clocks = ms_total, clocks
+    launches_per_step = launches / args.steps
+
+    # ------------------------------------------------------------ the same step as a CUDA graph
+    # One training step (forward and backward) captured once and replayed: the same kernels
+    # on the same buffers without the host's per-launch work.  The step has no host sync on
+    # one GPU and on the peer-memory transport (whose barriers keep their epochs on the
+    # device); the NCCL transport syncs with the host every step, so it runs eager.  Used by
+    # default for N > 1 on the peer-memory transport, where a rank's share of the step is
+    # short enough for launch overhead to matter.
+    use_graph = args.graph == "on" or (args.graph == "auto" and world > 1 and args.ep_transport == "nvlink")
+    if use_graph:
+        _progress("graph capture")
+        static_x = x.detach().clone().requires_grad_(True)
+        static_g = grad_out.clone()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                for p in layer.parameters():
+                    p.grad = None
+                static_x.grad = None
+                layer(static_x).backward(static_g)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for p in layer.parameters():
+            p.grad = None
+        static_x.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_out = layer(static_x)
+            static_out.backward(static_g)
+        for _ in range(3):
+            graph.replay()
+        barrier()
+        _progress("graph timed region")
+        sampler = ClockSampler(local)
+        sampler.start()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        g0.record()
+        for _ in range(args.steps):
+            graph.replay()
+        g1.record()
+        barrier()
+        clocks = sampler.stop()
+        ms_total = g0.elapsed_time(g1)
+        del static_out
 
     # ------------------------------------------------------------ end to end (host buffers)
     # Every step: the activations and the output gradient come from pinned host memory, and
@@ -422,6 +483,7 @@ def run_ours(args):
             gx_host.copy_(xin.grad, non_blocking=True)
         xin.grad.record_stream(d2h)
 
+    _progress("end-to-end region")
     e2e_step()
     torch.cuda.current_stream(dev).wait_stream(d2h)
     barrier()
@@ -436,19 +498,20 @@ def run_ours(args):
 
     # Device-side health after both timed regions: the library's error word (a bounded
     # wait that gave up, a refused slot) and, under EP, the peer barriers' status.
+    _progress("health and reduction")
     dev_err = _lib.read_device_error()
     healthy = layer.health_ok() if world > 1 else True
 
     # max over ranks (times, errors); every rank's live rows
-    t = torch.tensor([ms_total, e2e_ms, float(dev_err), 0.0 if healthy else 1.0, peak_mem_gb],
-                     device=dev, dtype=torch.float64)
+    t = torch.tensor([ms_total, e2e_ms, float(dev_err), 0.0 if healthy else 1.0, peak_mem_gb,
+                      eager_ms_total], device=dev, dtype=torch.float64)
     rows_all = [live_rows]
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         gath = [None] * world
         dist.all_gather_object(gath, live_rows)
         rows_all = gath
-    ms_total, e2e_ms, dev_err, unhealthy, peak_mem_gb = t.tolist()
+    ms_total, e2e_ms, dev_err, unhealthy, peak_mem_gb, eager_ms_total = t.tolist()
     ms_step = ms_total / args.steps
     value = flops_step * world / (ms_step * 1e-3) / 1e12
     e2e_value = flops_step * world / (e2e_ms / args.steps * 1e-3) / 1e12
@@ -490,7 +553,11 @@ def run_ours(args):
             "frac": round(achieved / peak, 4) if achieved else None,
             "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
             "live_rows_per_rank": rows_all,
-            "gemm_share_of_step": round(gemm_ms / ms_total, 4) if ms_total else None,
+            "gemm_share_of_step": round(gemm_ms / eager_ms_total, 4) if eager_ms_total else None,
+            "measured_on": "the eager timed region (per-launch CUDA events cannot be recorded "
+                           "inside a CUDA graph); same kernels and buffers as the graph replays"
+                           if use_graph else "the timed region",
+            "eager_clocks": eager_clocks if use_graph else None,
             "gemm_time_vs_roofline": round(t_roof * 1e3 / gemm_ms, 4) if gemm_ms else None,
             "roofline_note": "achieved = 9 GEMMs x 2*rows*d*H over the rows the experts computed "
                              "on (rank 0's, live_rows_per_rank[0]) / rank 0's summed GEMM launch "
@@ -511,7 +578,9 @@ def run_ours(args):
                     "copy stream (during the backward / the next forward); the last step's "
                     "copies finish inside the timed region",
         },
-        "gpu_launches": launches,
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "execution": ("CUDA graph of one fwd+bwd step, replayed" if use_graph else "eager"),
+        "eager_ms_per_step": round(eager_ms_total / args.steps, 4),
         "device_error": int(dev_err),
         "peer_barriers_ok": not unhealthy,
         "peak_mem_gb_per_rank": round(peak_mem_gb, 2),
@@ -796,6 +865,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="N = 1: leave out the per-op block")
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="time the step as a replayed CUDA graph (auto: N > 1 on the peer-memory "
+                         "transport, where the host's per-launch work would otherwise pace the "
+                         "short per-rank steps; one GPU measured no gain; the NCCL transport "
+                         "syncs with the host every step)")
     ap.add_argument("--cpu-sample-experts", type=int, default=8,
                     help="experts in the CPU baseline's sample (256 rows each)")
     args = ap.parse_args()

@@ -258,14 +258,22 @@ int moe_ep_combine_bwd(const void* grad_out, const void* const* in_bases, void* 
 int moe_add_rows(void* dst, const void* src, const int32_t* n_rows, int64_t max_rows,
                  int64_t num_cols, int dtype, void* stream);
 /* Cross-GPU barrier on `world` int64 flag arrays of `world` slots each (one per rank, in
- * IPC memory): writes `epoch` to slot `rank` of every rank's array (after a system-scope
- * fence), then waits until every slot of this rank's array reaches `epoch`.  Gives up after
- * timeout_ns: *status (device int32, may be NULL) = 0 and device error 4; a barrier that
- * completes leaves *status unchanged, so one status word records any failure over many
- * barriers.  Epochs must increase by one per barrier.  The ranks must run on different
- * GPUs. */
-int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t epoch,
+ * IPC memory).  The barrier's epoch is *epoch_counter + 1 (a device int64 of this rank,
+ * written back by the barrier, so a launch captured in a CUDA graph advances it on every
+ * replay; start it at 0 with the flags zeroed).  Writes the epoch to slot `rank` of every
+ * rank's array (after a system-scope fence), then waits until every slot of this rank's
+ * array reaches it.  Gives up after timeout_ns: *status (device int32, may be NULL) = 0 and
+ * device error 4; a barrier that completes leaves *status unchanged, so one status word
+ * records any failure over many barriers.  Every rank must run the same sequence of
+ * barriers.  The ranks must run on different GPUs. */
+int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t* epoch_counter,
                    uint64_t timeout_ns, int32_t* status, void* stream);
+/* Counts exchange of the peer-memory layout: counts[0..E) of this rank go to row `rank` of
+ * every rank's [world, E] int32 array (bases[r] is rank r's, mapped here).  A barrier must
+ * follow before any rank reads its array; no rank may write again before every rank has
+ * read (the layer's later barriers order that). */
+int moe_ep_put_counts(const int32_t* counts, int32_t num_experts, int32_t* const* bases,
+                      int32_t rank, int32_t world, void* stream);
 
 #ifdef __cplusplus
 }

@@ -45,7 +45,8 @@ SIGNATURES = {
     "moe_ep_combine_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_ptr, _c_ptr, _c_ptr, _c_int,
                                     _c_i64, _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr]),
     "moe_add_rows": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_i64, _c_i64, _c_int, _c_ptr]),
-    "moe_ep_barrier": (_c_int, [_c_ptr, _c_i32, _c_i32, _c_i64, ctypes.c_uint64, _c_ptr, _c_ptr]),
+    "moe_ep_barrier": (_c_int, [_c_ptr, _c_i32, _c_i32, _c_ptr, ctypes.c_uint64, _c_ptr, _c_ptr]),
+    "moe_ep_put_counts": (_c_int, [_c_ptr, _c_i32, _c_ptr, _c_i32, _c_i32, _c_ptr]),
     "moe_topk_softmax_fwd": (_c_int, [_c_ptr, _c_int, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr]),
     "moe_topk_softmax_bwd": (_c_int, [_c_ptr, _c_ptr, _c_ptr, _c_int, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr]),
     "moe_permute_workspace_bytes": (_c_size, [_c_i64, _c_i32, _c_i32]),

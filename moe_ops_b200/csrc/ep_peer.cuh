@@ -51,15 +51,19 @@ ep_slot_map_kernel(const int32_t* __restrict__ indices, const int32_t* __restric
   }
 }
 
-// One warp.  Lane i < world: make this rank's earlier writes visible system-wide, then
-// store `epoch` into slot `me` of rank i's flag array (a peer store over NVLink, or a local
-// one for i == me).  Then lane i waits until slot i of this rank's own array reaches
-// `epoch`, giving up after timeout_ns (device error 4, *status = 0; a barrier that completes
-// leaves *status as it was, so a failure stays visible).  Epochs increase by one per
-// barrier, so a flag never needs resetting.
+// One warp.  The barrier's epoch is this rank's device counter plus one (written back at the
+// end), so a launch captured in a CUDA graph advances it on every replay.  Lane i < world:
+// make this rank's earlier writes visible system-wide, then store the epoch into slot `me`
+// of rank i's flag array (a peer store over NVLink, or a local one for i == me).  Then lane
+// i waits until slot i of this rank's own array reaches the epoch, giving up after
+// timeout_ns (device error 4, *status = 0; a barrier that completes leaves *status as it
+// was, so a failure stays visible).  Epochs increase by one per barrier on every rank, so
+// a flag never needs resetting.
 __global__ void ep_barrier_kernel(int64_t* const* __restrict__ flags, int me, int world,
-                                  int64_t epoch, uint64_t timeout_ns, int32_t* __restrict__ status) {
+                                  int64_t* __restrict__ epoch_counter, uint64_t timeout_ns,
+                                  int32_t* __restrict__ status) {
   const int lane = threadIdx.x;
+  const int64_t epoch = *epoch_counter + 1;
   __threadfence_system();
   if (lane < world) {
     int64_t* slot = flags[lane] + me;
@@ -80,11 +84,25 @@ __global__ void ep_barrier_kernel(int64_t* const* __restrict__ flags, int me, in
     }
   }
   const bool all_ok = __all_sync(0xffffffffu, ok);
-  if (lane == 0 && !all_ok) {
-    raise_device_error(4);
-    if (status != nullptr) *status = 0;
+  if (lane == 0) {
+    *epoch_counter = epoch;
+    if (!all_ok) {
+      raise_device_error(4);
+      if (status != nullptr) *status = 0;
+    }
   }
   __threadfence_system();
+}
+
+// Counts exchange for the peer-memory layout: this rank's [E] counts go to row `me` of
+// every rank's [world, E] array (peer stores; the barrier that follows makes them visible).
+__global__ void __launch_bounds__(256)
+ep_put_counts_kernel(const int32_t* __restrict__ counts, int E, int32_t* const* __restrict__ dst,
+                     int me, int world) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < E * world; i += gridDim.x * blockDim.x) {
+    const int r = i / E, e = i - r * E;
+    dst[r][(int64_t)me * E + e] = counts[e];
+  }
 }
 
 // dst[r] = rnd(dst[r] + src[r]) for the first min(*n_rows, max_rows) rows (fp32 sum rounded

@@ -1112,12 +1112,24 @@ int moe_add_rows(void* dst, const void* src, const int32_t* n_rows, int64_t max_
   return MOE_OK;
 }
 
-int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t epoch,
+int moe_ep_barrier(int64_t* const* flags, int32_t rank, int32_t world, int64_t* epoch_counter,
                    uint64_t timeout_ns, int32_t* status, void* stream) {
-  MOE_REQUIRE(flags != nullptr && world > 0 && world <= 32 && rank >= 0 && rank < world && epoch > 0,
+  MOE_REQUIRE(flags != nullptr && epoch_counter != nullptr && world > 0 && world <= 32 &&
+                  rank >= 0 && rank < world,
               "ep_barrier: bad arguments rank=%d world=%d", rank, world);
   MOE_REQUIRE(timeout_ns <= 10000000000ull, "ep_barrier: timeout above 10 s");
-  ep_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, rank, world, epoch, timeout_ns, status);
+  ep_barrier_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(flags, rank, world, epoch_counter,
+                                                         timeout_ns, status);
+  MOE_LAUNCH_CHECK();
+  return MOE_OK;
+}
+
+int moe_ep_put_counts(const int32_t* counts, int32_t num_experts, int32_t* const* bases,
+                      int32_t rank, int32_t world, void* stream) {
+  MOE_REQUIRE(counts != nullptr && bases != nullptr && num_experts > 0 && world > 0 &&
+                  world <= 32 && rank >= 0 && rank < world,
+              "ep_put_counts: bad arguments E=%d rank=%d world=%d", num_experts, rank, world);
+  ep_put_counts_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(counts, num_experts, bases, rank, world);
   MOE_LAUNCH_CHECK();
   return MOE_OK;
 }

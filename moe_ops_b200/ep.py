@@ -218,7 +218,7 @@ class EPMoELayer(torch.nn.Module):
             self._peer = NVLinkTransport(self.group, capacity_rows(t_max, self.top_k, world),
                                          x.shape[1], x.dtype, x.device)
             self._peer_tokens = t_max
-        else:
+        elif not torch.cuda.is_current_stream_capturing():
             self._peer.check_health()
         if T > self._peer_tokens or x.shape[1] != self._peer.cols or x.dtype != self._peer.dtype:
             # Rebuilding here would be a collective that only this rank enters.

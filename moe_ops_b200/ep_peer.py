@@ -7,7 +7,7 @@ expert-major, then source-rank-major.
 
 Per layer step (rank r of W, El = E / W local experts):
 
-    forward   permute index pass (no copy) -> counts all-gather (NCCL, device only)
+    forward   permute index pass (no copy) -> counts exchange (peer stores + B0)
               -> delta / offsets (tiny tensor ops) -> slot map
               -> B1 -> dispatch: rows straight into the owners' receive buffers
               -> B2 -> gate/up + SwiGLU, down GEMMs into this rank's `down` buffer
@@ -20,6 +20,9 @@ Per layer step (rank r of W, El = E / W local experts):
 The barriers Bi are device-side (``moe_ep_barrier``). Waits are bounded, and every buffer
 reuse across ranks is ordered by one of them. For example, a rank's next dispatch into a
 peer's receive buffer waits at B1 until that peer's backward has finished reading it.
+Nothing in a step synchronises with the host or calls a collective library, and the
+barriers keep their epochs on the device, so a whole training step (forward and backward)
+can be captured in a CUDA graph and replayed.
 
 Results equal the single-GPU layer on the concatenated tokens bit for bit. An expert sees
 its rows in the same order (source rank, then stable slot order), and combine and its
@@ -39,6 +42,7 @@ import torch.distributed as dist
 from . import _lib
 
 _KINDS = ("recv", "down", "gdown", "dgrad")
+_MAX_COUNT_EXPERTS = 1024  # experts the counts exchange array holds
 
 
 def _as_tensor(ptr: int, shape: tuple, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
@@ -83,10 +87,12 @@ class NVLinkTransport(PeerTransport):
         self.capacity, self.cols, self.dtype = capacity, cols, dtype
         self.device = torch.device(device)
         self.timeout_ns = int(timeout_s * 1e9)
-        self.epoch = 0
         lib = _lib.load()
         es = torch.empty((), dtype=dtype).element_size()
-        sizes = [capacity * cols * es] * len(_KINDS) + [8 * self.world]
+        # the row buffers, the counts exchange array [world, kMaxCountExperts] int32, the
+        # barrier flags [world] int64
+        sizes = ([capacity * cols * es] * len(_KINDS) + [4 * self.world * _MAX_COUNT_EXPERTS]
+                 + [8 * self.world])
         self._own, handles = [], bytearray()
         with torch.cuda.device(self.device):
             for nbytes in sizes:
@@ -119,6 +125,10 @@ class NVLinkTransport(PeerTransport):
             self._flags = _as_tensor(self._own[-1], (self.world,), torch.int64, self.device)
             self._flags.zero_()
             self._flag_table = torch.tensor(table[-1], dtype=torch.int64, device=self.device)
+            self._epoch = torch.zeros(1, dtype=torch.int64, device=self.device)
+            self._counts = _as_tensor(self._own[-2], (self.world * _MAX_COUNT_EXPERTS,),
+                                      torch.int32, self.device)
+            self._counts_table = torch.tensor(table[-2], dtype=torch.int64, device=self.device)
             self._status = torch.ones(1, dtype=torch.int32, device=self.device)
             # Health of the previous steps, copied to pinned host memory at the end of every
             # backward and read (without a sync) at the start of a later forward.
@@ -136,15 +146,25 @@ class NVLinkTransport(PeerTransport):
         return self._status
 
     def all_gather_counts(self, counts):
-        out = torch.empty(self.world, counts.numel(), dtype=counts.dtype, device=counts.device)
-        dist.all_gather_into_tensor(out, counts.contiguous(), group=self.group)
-        return out
+        """Over peer memory, no collective library: this rank's counts go into row `rank` of
+        every rank's exchange array, then a barrier.  The returned [world, E] view is valid
+        until this rank's next call (every rank reads it before the step's later barriers)."""
+        E = counts.numel()
+        if E > _MAX_COUNT_EXPERTS:
+            raise ValueError(f"at most {_MAX_COUNT_EXPERTS} experts")
+        lib = _lib.load()
+        counts = counts.to(torch.int32).contiguous()
+        _lib.check(lib.moe_ep_put_counts(_lib.ptr(counts), E, _lib.ptr(self._counts_table),
+                                         self.rank, self.world, _lib.stream_of(counts)),
+                   "moe_ep_put_counts")
+        _lib.count_launches(1)
+        self.barrier()
+        return self._counts[: self.world * E].view(self.world, E)
 
     def barrier(self):
-        self.epoch += 1
         lib = _lib.load()
-        st = lib.moe_ep_barrier(_lib.ptr(self._flag_table), self.rank, self.world, self.epoch,
-                                self.timeout_ns, _lib.ptr(self._status),
+        st = lib.moe_ep_barrier(_lib.ptr(self._flag_table), self.rank, self.world,
+                                _lib.ptr(self._epoch), self.timeout_ns, _lib.ptr(self._status),
                                 _lib.stream_of(self._flag_table))
         _lib.check(st, "moe_ep_barrier")
         _lib.count_launches(1)
@@ -314,7 +334,7 @@ class _PeerExperts(torch.autograd.Function):
                    "moe_ep_combine")
         _lib.count_launches(3)
         tr.pending_backward = False
-        if hasattr(tr, "record_health"):
+        if hasattr(tr, "record_health") and not torch.cuda.is_current_stream_capturing():
             tr.record_health()
         return grad_x, grad_w, None, g_gate, g_up, g_down, None, None
 

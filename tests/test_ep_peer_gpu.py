@@ -178,18 +178,24 @@ def test_barrier_gives_up_on_a_silent_peer(cuda_dev):
     flags = [torch.zeros(2, dtype=torch.int64, device=cuda_dev) for _ in range(2)]
     table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=cuda_dev)
     status = torch.ones(1, dtype=torch.int32, device=cuda_dev)
-    # One rank alone: its own signal satisfies it, and the status stays 1.
+    epoch_a = torch.zeros(1, dtype=torch.int64, device=cuda_dev)
+    epoch_b = torch.zeros(1, dtype=torch.int64, device=cuda_dev)
+    # One rank alone: its own signal satisfies it, the status stays 1 and its epoch counter
+    # advances on the device.
     one = torch.tensor([flags[0].data_ptr()], dtype=torch.int64, device=cuda_dev)
-    assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, 1, 50_000_000, _lib.ptr(status), None) == 0
-    assert status.item() == 1
+    assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, _lib.ptr(epoch_a), 50_000_000, _lib.ptr(status),
+                              None) == 0
+    assert status.item() == 1 and epoch_a.item() == 1
     # Rank 0 of 2: rank 1 never signals, so the wait runs out after 50 ms.
-    assert lib.moe_ep_barrier(_lib.ptr(table), 0, 2, 1, 50_000_000, _lib.ptr(status), None) == 0
+    assert lib.moe_ep_barrier(_lib.ptr(table), 0, 2, _lib.ptr(epoch_b), 50_000_000, _lib.ptr(status),
+                              None) == 0
     assert status.item() == 0
     assert flags[1][0].item() == 1  # its own signal reached the silent peer's array
     assert _lib.read_device_error() == 4
     # A later barrier that completes leaves the failure recorded.
-    assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, 2, 50_000_000, _lib.ptr(status), None) == 0
-    assert status.item() == 0
+    assert lib.moe_ep_barrier(_lib.ptr(one), 0, 1, _lib.ptr(epoch_a), 50_000_000, _lib.ptr(status),
+                              None) == 0
+    assert status.item() == 0 and epoch_a.item() == 2
 
 
 def _free_port():
@@ -235,6 +241,31 @@ def _nvlink_worker(rank, world, port, q):
                 "grad_x": torch.equal(x.grad, ref_gx[rows]),
                 "grad_w": torch.equal(w_.grad, ref_gw[rows]),
                 "grad_experts": all(torch.equal(a.grad, b[sl]) for a, b in zip(ws, ref_gwe))}
+        # The same step captured in a CUDA graph (no host sync, barrier epochs on the device)
+        # and replayed twice: still bit-exact.
+        x = xs[rank].to(dev).requires_grad_(True)
+        w_, idx = M.fused_topk_softmax(logits[rank].to(dev), K)
+        w_ = w_.detach().requires_grad_(True)
+        ws = [t[sl].to(dev).requires_grad_(True) for t in (wg, wu, wd)]
+        g_out = gos[rank].to(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            peer_experts(x, w_, idx, *ws, tr, E).backward(g_out)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for t in (x, w_, *ws):
+            t.grad = None
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            gout = peer_experts(x, w_, idx, *ws, tr, E)
+            gout.backward(g_out)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        ok = ok and tr.barrier_ok() and _lib.read_device_error() == 0
+        same["graph_out"] = torch.equal(gout.detach(), ref_out[rows])
+        same["graph_grads"] = (torch.equal(x.grad, ref_gx[rows]) and torch.equal(w_.grad, ref_gw[rows])
+                               and all(torch.equal(a.grad, b[sl]) for a, b in zip(ws, ref_gwe)))
         q.put((rank, ok, same))
     finally:
         if tr is not None:
