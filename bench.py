@@ -398,6 +398,17 @@ def run_ours(args):
         t_roof += max(flop_s, mem_s)
     peak_mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
     eager_ms_total, eager_clocks = ms_total, clocks
+    # Per kind of grouped-GEMM launch: ms per step and TFLOP/s over the live rows.
+    by_kind = {}
+    for t in timing:
+        k = by_kind.setdefault(t[0], [0.0, 0.0, 0])
+        k[0] += t[1].elapsed_time(t[2])
+        k[1] += t[3] * scale
+        k[2] += 1
+    gemm_kinds = {name: {"launches_per_step": n // args.steps,
+                         "ms_per_step": round(ms / args.steps, 4),
+                         "tflops": round(fl / (ms * 1e-3) / 1e12, 1)}
+                  for name, (ms, fl, n) in sorted(by_kind.items())}
     launches_per_step = launches / args.steps
 
     # ------------------------------------------------------------ the same step as a CUDA graph
@@ -553,6 +564,7 @@ def run_ours(args):
             "frac": round(achieved / peak, 4) if achieved else None,
             "peak_kind": f"{peak_kind} bf16_tflops_sustained (kernel timed inside a long step)",
             "live_rows_per_rank": rows_all,
+            "by_launch_kind": gemm_kinds,
             "gemm_share_of_step": round(gemm_ms / eager_ms_total, 4) if eager_ms_total else None,
             "measured_on": "the eager timed region (per-launch CUDA events cannot be recorded "
                            "inside a CUDA graph); same kernels and buffers as the graph replays"

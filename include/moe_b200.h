@@ -95,6 +95,20 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
                 void* permuted, int32_t* row_id_map, int32_t* offsets, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* moe_permute with token dropping, the capacity case the reference leaves out
+ * (triton_gmm_ops/permute_ops.py:89-93 clamps num_out_tokens up to T*K instead).  Slots
+ * are ranked inside their expert in stable slot order (slot j = t*K + k: lower token
+ * first); a slot is kept while its rank is below `capacity` (<= 0: no per-expert limit)
+ * and its output row is below num_out (the rows of `permuted`).  A dropped slot gets
+ * row_id_map = -1 and no row; offsets [E+1] count the kept rows only (offsets[E] <=
+ * num_out), so grouped GEMMs over them never see a dropped slot, and moe_unpermute_fwd /
+ * _bwd treat -1 as an absent slot (it contributes zero; its prob_grad is zero).  Same
+ * workspace as moe_permute. */
+int moe_permute_capacity(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                         int32_t topk, int64_t num_cols, int32_t num_experts, int32_t capacity,
+                         int64_t num_out, void* permuted, int32_t* row_id_map, int32_t* offsets,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* SwiGLU between the expert GEMMs: out = silu(gate) * up over n elements, replacing the
  * reference layer's `F.silu(gate) * up` (tests/test_moe.py:82) and its autograd backward.
  * Rounding follows those PyTorch passes: silu rounded to dtype, then the product. */

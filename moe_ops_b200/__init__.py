@@ -12,6 +12,9 @@ libmoe_b200.so through its C ABI (include/moe_b200.h):
     unpermute_forward(...), unpermute_backward(...)
     fused_topk_softmax(logits, K, fp32_routing=False) -> (weights, indices)
 
+Beyond the reference: grouped_gemm_swiglu / grouped_swiglu_mlp (the SwiGLU expert MLP in
+fused launches) and permute_with_capacity (token dropping at a per-expert capacity).
+
 Layout conventions (same as the reference):
     A:        [total_tokens, K]   (all experts stacked along rows)
     B:        [E, N, K] if trans_b else [E, K, N]
@@ -20,7 +23,7 @@ Layout conventions (same as the reference):
     C:        [total_tokens, N]
 """
 from .grouped_gemm_ops import grouped_gemm, supports_tma
-from .permute_ops import permute, permute_backward
+from .permute_ops import permute, permute_backward, permute_with_capacity
 from .unpermute_ops import unpermute, unpermute_forward, unpermute_backward
 from .fused_topk_softmax_ops import fused_topk_softmax
 from .gate_up_ops import grouped_gemm_swiglu, grouped_swiglu_mlp
@@ -34,7 +37,8 @@ __all__ = [
     "unpermute_forward",
     "unpermute_backward",
     "fused_topk_softmax",
-    # beyond the reference's API: the SwiGLU expert MLP's fused launches
+    # beyond the reference's API: the SwiGLU expert MLP's fused launches, token dropping
     "grouped_gemm_swiglu",
+    "permute_with_capacity",
     "grouped_swiglu_mlp",
 ]

@@ -52,6 +52,9 @@ SIGNATURES = {
     "moe_permute_workspace_bytes": (_c_size, [_c_i64, _c_i32, _c_i32]),
     "moe_permute": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32, _c_i64,
                              _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size, _c_ptr]),
+    "moe_permute_capacity": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32,
+                                      _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size,
+                                      _c_ptr]),
     "moe_permute_noalloc": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32,
                                      _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr]),
     "moe_permute_noalloc_max_slots": (_c_size, [_c_i32]),

@@ -78,9 +78,19 @@ constexpr uint32_t kTmemCols = 2 * BN;
 constexpr uint32_t kEpiBufBytes = 32 * 64;  // 32 rows x 32 16-bit columns (swizzled 16-B chunks)
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;
 
+#ifndef MOE_CG2_STAGES
+#define MOE_CG2_STAGES 6
+#endif
+#ifndef MOE_CG2_EPI_BUFS
+#define MOE_CG2_EPI_BUFS 1
+#endif
+
 template <int CG>
 struct Shape {
-  static constexpr int STAGES = CG == 1 ? 4 : 6;
+  static constexpr int STAGES = CG == 1 ? 4 : MOE_CG2_STAGES;
+  // Epilogue staging buffers per warp: a warp's next 32 x 32 block goes into the next
+  // buffer while earlier TMA stores still read theirs.
+  static constexpr int EPI_BUFS = CG == 1 ? 1 : MOE_CG2_EPI_BUFS;
   static constexpr int TILE_M = BMC * CG;                     // rows of the tile (pair)
   static constexpr int B_COLS = BN / CG;                      // B columns held by one CTA
   static constexpr uint32_t A_BYTES = BMC * BK * 2;           // per CTA per stage
@@ -99,7 +109,7 @@ template <int CG>
 struct SmemLayout {
   uint8_t a[Shape<CG>::STAGES][Shape<CG>::A_BYTES];
   uint8_t b[Shape<CG>::STAGES][Shape<CG>::B_BYTES];
-  uint8_t cbuf[kEpiWarps][kEpiBufBytes];  // epilogue transpose buffers (one per warp)
+  uint8_t cbuf[kEpiWarps][Shape<CG>::EPI_BUFS][kEpiBufBytes];  // epilogue transpose buffers
   uint64_t full[Shape<CG>::STAGES];       // used in the leader CTA
   uint64_t empty[Shape<CG>::STAGES];
   uint64_t tmem_full[2];
@@ -600,11 +610,13 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     const int ew = warp - 4;
     const int q = ew & 3, h = ew >> 2;
     OutT* out = static_cast<OutT*>(p.out);
-    uint8_t* cbuf = s.cbuf[ew];
+    uint8_t* cbuf = &s.cbuf[ew][0][0];
     const int wr_row = lane;        // row written by this lane
     const int rd_chunk = lane & 3;  // 16-byte chunk read by this lane
     const int rd_row0 = lane >> 2;  // first row read by this lane (then +8, +16, +24)
     const uint32_t cbuf_u32 = ptx::smem_u32(cbuf);
+    constexpr int kBufs = Sh::EPI_BUFS;
+    int chunk_ctr = 0;  // 32 x 32 blocks this warp has staged (selects the buffer)
     int acc = 0;
     for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters, ++acc) {
       const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
@@ -778,13 +790,22 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
 #pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = 0u;
           }
-          // The previous TMA store from this buffer must have finished reading it.
-          if (lane == 0) ptx::bulk_wait_group_read<0>();
+          // The TMA store that last used this buffer must have finished reading it: with
+          // kBufs buffers in rotation, at most kBufs - 1 later stores may still be reading.
+          // The masked path below reads its buffer back without a store group, so it waits
+          // for all of them.
+          uint8_t* cb = cbuf + (chunk_ctr % kBufs) * kEpiBufBytes;
+          const uint32_t cb_u32 = cbuf_u32 + (uint32_t)((chunk_ctr % kBufs) * kEpiBufBytes);
+          ++chunk_ctr;
+          if (lane == 0) {
+            if (use_tma) ptx::bulk_wait_group_read<kBufs - 1>();
+            else ptx::bulk_wait_group_read<0>();
+          }
           __syncwarp();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int phys = i ^ ((wr_row >> 1) & 3);
-            *reinterpret_cast<uint4*>(cbuf + wr_row * 64 + phys * 16) =
+            *reinterpret_cast<uint4*>(cb + wr_row * 64 + phys * 16) =
                 make_uint4(w[i * 4 + 0], w[i * 4 + 1], w[i * 4 + 2], w[i * 4 + 3]);
           }
           if (use_tma) {
@@ -792,8 +813,8 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             __syncwarp();
             if (lane == 0) {
               const int cx = n0 + col_lo + c * 32;
-              if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cbuf_u32, cx, row_base + rq * 32);
-              else ptx::tma_store_3d(&map_c, cbuf_u32, cx, row_base + rq * 32, ti.g);
+              if (MODE == kModeRows) ptx::tma_store_2d(&map_c, cb_u32, cx, row_base + rq * 32);
+              else ptx::tma_store_3d(&map_c, cb_u32, cx, row_base + rq * 32, ti.g);
               ptx::bulk_commit_group();
             }
             if (has_acc && c + 1 < nchunks) ptx::tmem_wait_ld();
@@ -805,7 +826,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
           for (int i = 0; i < 4; ++i) {
             const int rr = rd_row0 + i * 8;
             const int phys = rd_chunk ^ ((rr >> 1) & 3);
-            const uint4 u = *reinterpret_cast<const uint4*>(cbuf + rr * 64 + phys * 16);
+            const uint4 u = *reinterpret_cast<const uint4*>(cb + rr * 64 + phys * 16);
             const int row = rq * 32 + rr;
             if (row < valid_rows && col < valid_cols)
               *reinterpret_cast<uint4*>(tile_ptr + (int64_t)row * p.n_out + col) = u;

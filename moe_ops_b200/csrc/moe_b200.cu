@@ -498,18 +498,16 @@ size_t moe_permute_workspace_bytes(int64_t num_tokens, int32_t topk, int32_t E) 
   return permute_ws(num_tokens, topk, E).total_bytes;
 }
 
-int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
-                int32_t topk, int64_t num_cols, int32_t E, int64_t num_out, void* permuted,
-                int32_t* row_id_map, int32_t* offsets, void* workspace, size_t workspace_bytes,
-                void* stream) {
-  MOE_REQUIRE(dtype_ok(dtype), "permute: bad dtype %d", dtype);
-  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0,
-              "permute: bad sizes T=%lld K=%d C=%lld", (long long)num_tokens, topk, (long long)num_cols);
-  MOE_REQUIRE(E > 0 && E <= kMaxExperts, "permute: need 0 < E <= %d (E=%d)", kMaxExperts, E);
+}  // extern "C"
+
+namespace moe {
+// The counting-sort permute with optional dropping (see permute_rank_kernel): a slot is
+// kept while its rank inside its expert is below `capacity` and its row below `row_limit`.
+static int permute_impl(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                        int32_t topk, int64_t num_cols, int32_t E, int32_t capacity,
+                        int32_t row_limit, void* permuted, int32_t* row_id_map, int32_t* offsets,
+                        void* workspace, size_t workspace_bytes, void* stream) {
   const int64_t num_slots = num_tokens * topk;
-  MOE_REQUIRE(num_out >= num_slots, "permute: num_out (%lld) < T*K (%lld)", (long long)num_out,
-              (long long)num_slots);
-  MOE_REQUIRE(num_slots < (1ll << 31), "permute: T*K must fit in int32");
   cudaStream_t s = (cudaStream_t)stream;
   if (num_slots == 0) {
     MOE_CUDA_CHECK(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), s));
@@ -524,7 +522,7 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   permute_hist_kernel<<<tiles, kPermTile, E * sizeof(int32_t), s>>>(indices, num_slots, E, cnt,
                                                                      w.num_tiles);
   MOE_LAUNCH_CHECK();
-  const size_t rank_smem = (size_t)(kPermTileWarps + 2) * E * sizeof(int32_t);
+  const size_t rank_smem = (size_t)(kPermTileWarps + 3) * E * sizeof(int32_t);
   if (rank_smem > 48 * 1024) {
     // The opt-in limit only grows, so a concurrent call with a smaller E never lowers it
     // under a launch that needs more.
@@ -539,7 +537,8 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
     }
   }
   permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
-                                                          cnt, w.num_tiles, row_id_map, offsets);
+                                                          cnt, w.num_tiles, row_id_map, offsets,
+                                                          capacity, row_limit);
   MOE_LAUNCH_CHECK();
   if (num_cols == 0) return MOE_OK;
   const int es = dtype_size(dtype);
@@ -563,6 +562,43 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
 #undef MOE_COPY
   MOE_LAUNCH_CHECK();
   return MOE_OK;
+}
+}  // namespace moe
+
+extern "C" {
+
+int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                int32_t topk, int64_t num_cols, int32_t E, int64_t num_out, void* permuted,
+                int32_t* row_id_map, int32_t* offsets, void* workspace, size_t workspace_bytes,
+                void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "permute: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0,
+              "permute: bad sizes T=%lld K=%d C=%lld", (long long)num_tokens, topk, (long long)num_cols);
+  MOE_REQUIRE(E > 0 && E <= kMaxExperts, "permute: need 0 < E <= %d (E=%d)", kMaxExperts, E);
+  const int64_t num_slots = num_tokens * topk;
+  MOE_REQUIRE(num_out >= num_slots, "permute: num_out (%lld) < T*K (%lld)", (long long)num_out,
+              (long long)num_slots);
+  MOE_REQUIRE(num_slots < (1ll << 31), "permute: T*K must fit in int32");
+  return permute_impl(input, dtype, indices, num_tokens, topk, num_cols, E, INT32_MAX, INT32_MAX,
+                      permuted, row_id_map, offsets, workspace, workspace_bytes, stream);
+}
+
+int moe_permute_capacity(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
+                         int32_t topk, int64_t num_cols, int32_t E, int32_t capacity,
+                         int64_t num_out, void* permuted, int32_t* row_id_map, int32_t* offsets,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  MOE_REQUIRE(dtype_ok(dtype), "permute_capacity: bad dtype %d", dtype);
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32 && num_cols >= 0,
+              "permute_capacity: bad sizes T=%lld K=%d C=%lld", (long long)num_tokens, topk,
+              (long long)num_cols);
+  MOE_REQUIRE(E > 0 && E <= kMaxExperts, "permute_capacity: need 0 < E <= %d (E=%d)", kMaxExperts, E);
+  const int64_t num_slots = num_tokens * topk;
+  MOE_REQUIRE(num_slots < (1ll << 31), "permute_capacity: T*K must fit in int32");
+  MOE_REQUIRE(num_out >= 0 && num_out < (1ll << 31), "permute_capacity: bad num_out %lld",
+              (long long)num_out);
+  return permute_impl(input, dtype, indices, num_tokens, topk, num_cols, E,
+                      capacity > 0 ? capacity : INT32_MAX, (int32_t)num_out, permuted, row_id_map,
+                      offsets, workspace, workspace_bytes, stream);
 }
 
 int moe_swiglu_fwd(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream) {

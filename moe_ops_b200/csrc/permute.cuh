@@ -55,14 +55,21 @@ permute_hist_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int E,
 //   base[e] = offsets[e] + sum_{t < tile} cnt[e][t],  offsets[e] = sum_{e' < e, all t} cnt.
 // Block 0 also writes offsets[E+1].  Then the tile's slots are ranked stably: warp match for
 // the rank inside a warp, a per-warp column scan across the warps of the tile.
-// Dynamic shared memory: (kPermTileWarps + 2) * E int32.
+//
+// Capacity (dropping): a slot whose stable rank inside its expert is >= `capacity`, or
+// whose destination row would be >= `row_limit`, is dropped: row_id_map = -1 and no row.
+// The offsets count the kept rows only, so the grouped GEMMs never see a dropped slot.
+// Both limits at INT32_MAX give the plain permute.
+// Dynamic shared memory: (kPermTileWarps + 3) * E int32.
 __global__ void __launch_bounds__(kPermTile)
 permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t num_tokens,
                     int K, int E, const int32_t* __restrict__ cnt, int64_t num_tiles,
-                    int32_t* __restrict__ row_id_map, int32_t* __restrict__ offsets) {
+                    int32_t* __restrict__ row_id_map, int32_t* __restrict__ offsets,
+                    int32_t capacity, int32_t row_limit) {
   extern __shared__ int32_t s_cnt[];     // [kPermTileWarps][E]
   int32_t* s_before = s_cnt + kPermTileWarps * E;  // [E] this expert's rows in earlier tiles
   int32_t* s_total = s_before + E;                 // [E] this expert's rows in all tiles
+  int32_t* s_first = s_total + E;                  // [E] first output row of the expert
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
   for (int i = threadIdx.x; i < kPermTileWarps * E; i += blockDim.x) s_cnt[i] = 0;
@@ -82,12 +89,12 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
     if (lane == 0) { s_before[x] = before; s_total[x] = total; }
   }
   __syncthreads();
-  // Exclusive prefix of the totals over experts (one warp; E <= kMaxExperts).
+  // Exclusive prefix of the kept totals over experts (one warp; E <= kMaxExperts).
   if (warp == 0) {
     int32_t carry = 0;
     for (int x0 = 0; x0 < E; x0 += 32) {
       const int x = x0 + lane;
-      const int32_t v = x < E ? s_total[x] : 0;
+      const int32_t v = x < E ? min(s_total[x], capacity) : 0;
       int32_t inc = v;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -95,13 +102,13 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
         if (lane >= off) inc += o;
       }
       if (x < E) {
-        const int32_t first = carry + inc - v;  // offsets[x]
-        if (tile == 0) offsets[x] = first;
-        s_before[x] += first;
+        const int32_t first = carry + inc - v;  // offsets[x] before the row limit
+        if (tile == 0) offsets[x] = min(first, row_limit);
+        s_first[x] = first;
       }
       carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    if (tile == 0 && lane == 0) offsets[E] = carry;
+    if (tile == 0 && lane == 0) offsets[E] = min(carry, row_limit);
   }
   const int64_t j = tile * kPermTile + threadIdx.x;
   int e = -1;
@@ -126,7 +133,12 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
   __syncthreads();
   if (j < num_slots) {
     const int64_t t = j / K, k = j - t * K;
-    row_id_map[k * num_tokens + t] = e >= 0 ? s_cnt[warp * E + e] + intra : -1;
+    int32_t dst = -1;
+    if (e >= 0) {
+      const int32_t r = s_cnt[warp * E + e] + intra;  // stable rank inside expert e
+      if (r < capacity && s_first[e] + r < row_limit) dst = s_first[e] + r;
+    }
+    row_id_map[k * num_tokens + t] = dst;
   }
 }
 

@@ -19,21 +19,27 @@ import torch
 
 from .fused_topk_softmax_ops import fused_topk_softmax
 from .gate_up_ops import grouped_swiglu_mlp
-from .permute_ops import permute
+from .permute_ops import permute, permute_with_capacity
 from .unpermute_ops import unpermute
 
 
 def moe_layer_forward(x: torch.Tensor, w_router: torch.Tensor, w_gate: torch.Tensor,
                       w_up: torch.Tensor, w_down: torch.Tensor, top_k: int,
                       fp32_routing: bool = False,
-                      router_bias: torch.Tensor | None = None) -> torch.Tensor:
+                      router_bias: torch.Tensor | None = None,
+                      capacity: int = 0) -> torch.Tensor:
+    """capacity > 0: each expert takes at most that many slots (its first in token order);
+    a dropped slot adds nothing to its token's output (permute_with_capacity)."""
     E = w_gate.shape[0]
     num_tokens = x.shape[0]
     logits = x @ w_router.t()
     if router_bias is not None:
         logits = logits + router_bias
     weights, indices = fused_topk_softmax(logits, top_k, fp32_routing=fp32_routing)
-    permuted, row_id_map, offsets = permute(x, indices, E=E)
+    if capacity > 0:
+        permuted, row_id_map, offsets = permute_with_capacity(x, indices, E, capacity)
+    else:
+        permuted, row_id_map, offsets = permute(x, indices, E=E)
     down = grouped_swiglu_mlp(permuted, w_gate, w_up, w_down, offsets, trans_b=True)
     return unpermute(down, row_id_map, weights, num_tokens, top_k)
 
@@ -53,6 +59,8 @@ class MoELayer(torch.nn.Module):
         self.w_up = torch.nn.Parameter(torch.empty(num_experts, hidden, d_model, **kw))
         self.w_down = torch.nn.Parameter(torch.empty(num_experts, d_model, hidden, **kw))
         self.router_bias = None  # optional fixed per-expert logit bias [E]
+        # > 0: expert capacity = ceil(capacity_factor * T * K / E) slots (token dropping)
+        self.capacity_factor = 0.0
 
     @torch.no_grad()
     def init_normal(self, std: float = 0.02, generator=None) -> "MoELayer":
@@ -61,8 +69,11 @@ class MoELayer(torch.nn.Module):
         return self
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        cap = 0
+        if self.capacity_factor > 0:
+            cap = -(-int(self.capacity_factor * x.shape[0] * self.top_k) // self.num_experts)
         return moe_layer_forward(x, self.w_router, self.w_gate, self.w_up, self.w_down,
-                                 self.top_k, self.fp32_routing, self.router_bias)
+                                 self.top_k, self.fp32_routing, self.router_bias, cap)
 
 
 def layer_gemm_flops(num_tokens: int, top_k: int, d_model: int, hidden: int,

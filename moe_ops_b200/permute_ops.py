@@ -103,6 +103,88 @@ def permute(input, indices, num_out_tokens=0, E=None):
     return PermuteAutograd.apply(input, indices, num_out_tokens, E)
 
 
+# ---------------------------------------------------------------- permute with dropping
+
+
+def capacity_rows(num_slots: int, num_experts: int, capacity: int, num_out_tokens: int) -> int:
+    """Rows of the permuted buffer of permute_with_capacity (known on the host, no sync):
+    num_out_tokens if given, else the most rows the capacity can keep."""
+    if num_out_tokens > 0:
+        return num_out_tokens
+    if capacity > 0:
+        return min(num_slots, num_experts * capacity)
+    return num_slots
+
+
+@torch.library.custom_op(f"{_NS}::permute_capacity", mutates_args=())
+def permute_capacity(input: torch.Tensor, indices: torch.Tensor, E: int, capacity: int = 0,
+                     num_out_tokens: int = 0) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Counting-sort permute that drops slots past an expert's capacity (the first
+    `capacity` slots of each expert in token order are kept) or past num_out_tokens rows."""
+    _lib.require_cuda(input, indices)
+    input = input.contiguous()
+    if indices.dim() == 1:
+        indices = indices.unsqueeze(1)
+    num_tokens, num_cols = input.shape
+    topK = indices.shape[1]
+    flat = indices.reshape(-1).to(torch.int32).contiguous()
+    num_out = capacity_rows(num_tokens * topK, E, capacity, num_out_tokens)
+    lib = _lib.load()
+    permuted = torch.empty(num_out, num_cols, device=input.device, dtype=input.dtype)
+    row_id_map = torch.empty(num_tokens * topK, dtype=torch.int32, device=input.device)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=input.device)
+    ws_bytes = lib.moe_permute_workspace_bytes(num_tokens, topK, E)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=input.device)
+    with torch.cuda.device(input.device):
+        st = lib.moe_permute_capacity(
+            _lib.ptr(input), _lib.dtype_code(input.dtype), _lib.ptr(flat), num_tokens, topK,
+            num_cols, E, capacity, num_out, _lib.ptr(permuted), _lib.ptr(row_id_map),
+            _lib.ptr(offsets), _lib.ptr(ws), ws_bytes, _lib.stream_of(input))
+    _lib.check(st, "moe_permute_capacity")
+    _lib.count_launches(3)
+    return permuted, row_id_map, offsets
+
+
+@permute_capacity.register_fake
+def _(input, indices, E, capacity=0, num_out_tokens=0):
+    num_tokens, num_cols = input.shape
+    topK = indices.shape[1] if indices.dim() > 1 else 1
+    num_out = capacity_rows(num_tokens * topK, E, capacity, num_out_tokens)
+    return (torch.empty(num_out, num_cols, device=input.device, dtype=input.dtype),
+            torch.empty(num_tokens * topK, device=input.device, dtype=torch.int32),
+            torch.empty(E + 1, device=input.device, dtype=torch.int32))
+
+
+class PermuteCapacityAutograd(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, input, indices, E, capacity, num_out_tokens):
+        ctx.num_tokens = input.shape[0]
+        ctx.topK = indices.shape[1] if indices.ndim > 1 else 1
+        permuted, row_id_map, offsets = torch.ops.moeb200.permute_capacity(
+            input, indices, E, capacity, num_out_tokens)
+        ctx.save_for_backward(row_id_map)
+        ctx.mark_non_differentiable(row_id_map, offsets)
+        return permuted, row_id_map, offsets
+
+    @staticmethod
+    def backward(ctx, grad_permuted, grad_row_id_map, grad_offsets):
+        (row_id_map,) = ctx.saved_tensors
+        # dropped slots (row -1) contribute nothing
+        grad_input = permute_backward(grad_permuted, row_id_map, ctx.num_tokens, ctx.topK)
+        return grad_input, None, None, None, None
+
+
+def permute_with_capacity(input, indices, E: int, capacity: int = 0, num_out_tokens: int = 0):
+    """Differentiable permute with token dropping; returns (permuted, row_id_map, offsets)
+    as permute() does.  Each expert keeps its first `capacity` slots in token order
+    (capacity <= 0: all); with num_out_tokens > 0 the permuted buffer has that many rows and
+    slots whose row would fall past it are dropped too (the highest experts' last slots
+    first).  Dropped slots have row_id_map = -1: unpermute gives them zero weight in the
+    output and a zero routing-weight gradient.  The reference's permute has no dropping
+    (permute_ops.py:89-93 raises num_out_tokens to T*K); permute() here keeps that contract."""
+    return PermuteCapacityAutograd.apply(input, indices, E, capacity, num_out_tokens)
+
+
 # ---------------------------------------------------------------- rows through a given map
 
 

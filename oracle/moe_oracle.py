@@ -117,6 +117,45 @@ def permute(input: torch.Tensor, indices: torch.Tensor, E: int | None = None,
     return permuted, torch.from_numpy(row_id_map), torch.from_numpy(group_offsets(flat, E))
 
 
+def permute_capacity(input: torch.Tensor, indices: torch.Tensor, E: int, capacity: int = 0,
+                     num_out_tokens: int = 0) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Capacity dropping, which the reference leaves out (permute_ops.py:89-93 raises
+    num_out_tokens to T*K): this library's definition, restated plainly.  Slots in stable
+    argsort order of the flattened expert ids (as permute above); inside each expert the
+    first `capacity` slots (lowest t*K + k) are kept (capacity <= 0: all), the kept slots are
+    laid out expert by expert, and slots whose row would be >= num_out (> 0) are dropped
+    too.  Dropped slots get row -1.  Returns (permuted [num_out or kept rows, C],
+    row_id_map [K*T], offsets [E+1] of the kept rows)."""
+    T, C = input.shape
+    ind = indices.reshape(T, -1)
+    K = ind.shape[1]
+    flat = ind.reshape(-1).numpy().astype(np.int64)
+    order = np.argsort(flat, kind="stable")
+    cap = capacity if capacity > 0 else T * K
+    row_id_map = np.full(T * K, -1, dtype=np.int32)
+    counts = np.zeros(E, dtype=np.int64)
+    kept = []
+    for j in order:  # expert by expert, stable inside each
+        e = flat[j]
+        if counts[e] < cap:
+            counts[e] += 1
+            kept.append(j)
+    if num_out_tokens > 0:
+        kept = kept[:num_out_tokens]
+        rows = num_out_tokens
+    else:
+        rows = min(T * K, E * capacity) if capacity > 0 else T * K
+    permuted = torch.zeros(rows, C, dtype=input.dtype)
+    kept = np.asarray(kept, dtype=np.int64)
+    if kept.size:
+        permuted[: kept.size] = input[torch.from_numpy(kept // K)]
+        row_id_map[(kept % K) * T + kept // K] = np.arange(kept.size, dtype=np.int32)
+    kept_counts = np.bincount(flat[kept], minlength=E) if kept.size else np.zeros(E, np.int64)
+    offsets = np.zeros(E + 1, dtype=np.int32)
+    offsets[1:] = np.cumsum(kept_counts)
+    return permuted, torch.from_numpy(row_id_map), torch.from_numpy(offsets)
+
+
 # ----------------------------------------------------------------------------- unpermute
 
 

@@ -130,6 +130,8 @@ def test_every_custom_op_has_a_fake_impl():
             "permute_countsort": (ops.permute_countsort(x, idx, 0, E),
                                   [((T * K, d), bf), ((T * K,), torch.int32), ((E + 1,), torch.int32)]),
             "scatter_rows": (ops.scatter_rows(x, rid, T * K, K), [((T * K, d), bf)]),
+            "permute_capacity": (ops.permute_capacity(x, idx, E, 5, 0),
+                                 [((E * 5, d), bf), ((T * K,), torch.int32), ((E + 1,), torch.int32)]),
             "unpermute_forward": (ops.unpermute_forward(A, rid, prob, T, K), [((T, d), bf)]),
             "unpermute_backward": (ops.unpermute_backward(x, A, rid, prob, T, K),
                                    [((T * K, d), bf), ((T, K), torch.float32)]),

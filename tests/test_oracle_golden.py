@@ -78,3 +78,20 @@ def test_cfg1_layer_oracle_matches_reference():
     assert abs(loss.item() - float(g["loss"])) <= 1e-4 * abs(float(g["loss"]))
     assert O.rel_frobenius(x.grad, g["grad_x"]) < 1e-4
     assert O.rel_frobenius(wr.grad, g["grad_router"]) < 1e-4
+
+
+def test_capacity_oracle_hand_case():
+    """The dropping definition on a case worked by hand: T=4, K=2, E=3, capacity 2.
+    Slots j = t*K+k route to experts [0,1 | 0,2 | 0,1 | 1,2].  Expert 0 has slots 0,2,4 and
+    keeps 0,2; expert 1 has 1,5,6 and keeps 1,5; expert 2 has 3,7 and keeps both."""
+    x = torch.arange(4 * 2, dtype=torch.float32).view(4, 2)
+    idx = torch.tensor([[0, 1], [0, 2], [0, 1], [1, 2]], dtype=torch.int32)
+    p, r, o = O.permute_capacity(x, idx, 3, capacity=2)
+    assert o.tolist() == [0, 2, 4, 6]
+    assert r.tolist() == [0, 1, -1, -1, 2, 4, 3, 5]  # row_id_map[k*T + t]
+    assert [int(v) for v in p[:, 0] // 2] == [0, 1, 0, 2, 1, 3]  # tokens of the kept rows
+    # a global budget of 5 rows also drops the last kept slot (expert 2, token 3)
+    p5, r5, o5 = O.permute_capacity(x, idx, 3, capacity=2, num_out_tokens=5)
+    assert o5.tolist() == [0, 2, 4, 5]
+    assert r5.tolist() == [0, 1, -1, -1, 2, 4, 3, -1]
+    assert p5.shape[0] == 5
