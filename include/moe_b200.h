@@ -109,6 +109,16 @@ int moe_permute_capacity(const void* input, int dtype, const int32_t* indices, i
                          int64_t num_out, void* permuted, int32_t* row_id_map, int32_t* offsets,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Index pass of moe_permute (no rows copied) that also writes the inverse map:
+ * row_src[row] = the token whose slot lands in that permuted row ([T*K] int32).  With it
+ * the grouped GEMMs can read the permuted operand straight from the token-order input
+ * (moe_gmm_*_gather), so the permuted copy is never written: the fused permute -> GEMM of
+ * the reference's experiment (develop/experiment/fused_ops.py:31-107, rows fetched through
+ * `sorted_id_map`).  row_id_map / offsets as moe_permute; workspace as moe_permute. */
+int moe_permute_index(const int32_t* indices, int64_t num_tokens, int32_t topk, int32_t num_experts,
+                      int32_t* row_id_map, int32_t* offsets, int32_t* row_src, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* SwiGLU between the expert GEMMs: out = silu(gate) * up over n elements, replacing the
  * reference layer's `F.silu(gate) * up` (tests/test_moe.py:82) and its autograd backward.
  * Rounding follows those PyTorch passes: silu rounded to dtype, then the product. */
@@ -197,6 +207,26 @@ int moe_gmm_dgrad_dual(const void* grad_C1, const void* B1, const void* grad_C2,
 int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t* offsets,
                   int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
                   int32_t num_experts, int trans_b, int dtype, void* stream);
+
+/* Gathered-A forms (permute fused into the GEMM, develop/experiment/fused_ops.py:31-107 and
+ * its weight gradient): row r of A is row a_rows[r] of A_src [a_src_rows, k] (a_rows from
+ * moe_permute_index), fetched with TMA gather4, so the permuted copy of A is never
+ * materialised.  Results equal moe_gmm_fwd / moe_gmm_gate_up_fwd / moe_gmm_wgrad on the
+ * materialised permuted A bit for bit.  Tensor-core path only (16-bit, 16-byte aligned,
+ * sizes multiples of 8; MOE_ERR_INVALID_ARG otherwise); wgrad_gather takes trans_b only. */
+int moe_gmm_fwd_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows, const void* B,
+                       void* C, const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                       int64_t n, int64_t k, int32_t num_experts, int trans_b, int dtype,
+                       void* stream);
+int moe_gmm_gate_up_fwd_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows,
+                               const void* B_gate, const void* B_up, void* gate, void* up, void* h,
+                               const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                               int64_t n, int64_t k, int32_t num_experts, int trans_b, int dtype,
+                               void* stream);
+int moe_gmm_wgrad_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows,
+                         const void* grad_C, void* grad_B, const int32_t* offsets,
+                         int32_t num_offsets, int64_t m_total, int64_t n, int64_t k,
+                         int32_t num_experts, int trans_b, int dtype, void* stream);
 
 /* Gate and up projections of a SwiGLU expert layer with the SwiGLU applied, in one launch:
  *   gate = A @ B_gate[e]^T, up = A @ B_up[e]^T (trans_b; else A @ B[e]),

@@ -13,7 +13,8 @@ libmoe_b200.so through its C ABI (include/moe_b200.h):
     fused_topk_softmax(logits, K, fp32_routing=False) -> (weights, indices)
 
 Beyond the reference: grouped_gemm_swiglu / grouped_swiglu_mlp (the SwiGLU expert MLP in
-fused launches) and permute_with_capacity (token dropping at a per-expert capacity).
+fused launches), permute_with_capacity (token dropping at a per-expert capacity), and
+permute_index + grouped_swiglu_mlp_gathered (the permute fused into the expert GEMMs).
 
 Layout conventions (same as the reference):
     A:        [total_tokens, K]   (all experts stacked along rows)
@@ -27,6 +28,7 @@ from .permute_ops import permute, permute_backward, permute_with_capacity
 from .unpermute_ops import unpermute, unpermute_forward, unpermute_backward
 from .fused_topk_softmax_ops import fused_topk_softmax
 from .gate_up_ops import grouped_gemm_swiglu, grouped_swiglu_mlp
+from .fused_permute_ops import grouped_swiglu_mlp_gathered, permute_index
 
 __all__ = [
     "grouped_gemm",
@@ -40,5 +42,8 @@ __all__ = [
     # beyond the reference's API: the SwiGLU expert MLP's fused launches, token dropping
     "grouped_gemm_swiglu",
     "permute_with_capacity",
+    # the permute fused into the expert GEMMs (rows gathered from x, no permuted copy)
+    "permute_index",
+    "grouped_swiglu_mlp_gathered",
     "grouped_swiglu_mlp",
 ]

@@ -55,6 +55,15 @@ SIGNATURES = {
     "moe_permute_capacity": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32,
                                       _c_i32, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr, _c_size,
                                       _c_ptr]),
+    "moe_permute_index": (_c_int, [_c_ptr, _c_i64, _c_i32, _c_i32, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                   _c_size, _c_ptr]),
+    "moe_gmm_fwd_gather": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64,
+                                    _c_i64, _c_i64, _c_i32, _c_int, _c_int, _c_ptr]),
+    "moe_gmm_gate_up_fwd_gather": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr,
+                                            _c_ptr, _c_ptr, _c_i32, _c_i64, _c_i64, _c_i64, _c_i32,
+                                            _c_int, _c_int, _c_ptr]),
+    "moe_gmm_wgrad_gather": (_c_int, [_c_ptr, _c_ptr, _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_i32, _c_i64,
+                                      _c_i64, _c_i64, _c_i32, _c_int, _c_int, _c_ptr]),
     "moe_permute_noalloc": (_c_int, [_c_ptr, _c_int, _c_ptr, _c_i64, _c_i32, _c_i64, _c_i32,
                                      _c_i64, _c_ptr, _c_ptr, _c_ptr, _c_ptr]),
     "moe_permute_noalloc_max_slots": (_c_size, [_c_i32]),

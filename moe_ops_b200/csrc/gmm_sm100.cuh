@@ -140,6 +140,11 @@ struct Params {
   const void* in_gate;   // kModeSwiGLUBwd: the forward's gate [m_total, n_out]
   const void* in_up;     // kModeSwiGLUBwd: the forward's up [m_total, n_out]
   int q_fastest;         // kModeWgrad: walk an expert's tiles output-column block fastest
+  // Gathered operand (permute fused into the GEMM): row r of the operand is row
+  // gather_rows[r] of a [gather_src_rows, ...] tensor, fetched with TMA gather4 (the map's
+  // box is one row high).  Row mode (1-SM tiles): the operand is A; wgrad mode: Y.
+  const int32_t* gather_rows;
+  int gather_src_rows;
   int k_red2;            // kModeRows: > 0 adds a second contraction segment into the same
                          // accumulator: C = A . op(B[g]) + A2 . op(B2[g]), A2 [m_total,
                          // k_red2] through map_c2 and B2 through map_b2 (two-segment dgrad)
@@ -402,10 +407,29 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
     // handed to the fix-up warp, the producer moves on to the next stage.
     int stage = 0;
     uint32_t phase = 0;
+    const bool gather = p.gather_rows != nullptr;
+    // A source row of the gathered operand, clamped into the tensor (rows past the data
+    // are never stored: row tiles mask them and wgrad zeroes them).
+    auto src_row = [&](int r) {
+      r = min(max(r, 0), (int)p.m_total - 1);
+      const int v = __ldg(p.gather_rows + r);
+      return min(max(v, 0), p.gather_src_rows - 1);
+    };
     for (int t = cluster_id; t < total_tiles && !*abort_flag; t += num_clusters) {
       const TileInfo ti = decode_tile<MODE, CG>(s.tile_prefix, p, t);
+      int grow[4] = {0, 0, 0, 0};  // row tiles: this lane's 4 rows of the tile's A block
+      if (MODE != kModeWgrad && gather) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) grow[i] = src_row(ti.row0 + lane * 4 + i);
+      }
       for (int kb = 0; kb < ti.nkb; ++kb) {
         if (!wait_local(ptx::smem_u32(&s.empty[stage]), phase ^ 1, abort_flag)) break;
+        if (MODE == kModeWgrad && gather) {
+          // this lane's 4 contraction rows of the k-block (16 groups of 4 per 64 rows)
+          const int r = ti.row0 + kb * BK + (lane & 15) * 4;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) grow[i] = src_row(r + i);
+        }
         if (lane == 0) {
           const uint32_t sa = ptx::smem_u32(&s.a[stage][0]);
           const uint32_t sb = ptx::smem_u32(&s.b[stage][0]);
@@ -430,7 +454,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             const CUtensorMap* mapB = seg2 ? &map_b2 : &map_b;
             const int nb = ti.n_blk * tile_out_cols<MODE>() + (int)rank * Sh::B_COLS;
             const int a_rows = half ? BMC / 2 : BMC;
-            for (int j = 0; j < a_rows / 64; ++j) {
+            for (int j = 0; j < a_rows / 64 && !gather; ++j) {
               const int ar = ti.row0 + (int)rank * a_rows + j * 64;
               if (CG == 1) ptx::tma_load_2d(sa + j * (64 * 128), mapA, full_c, k0, ar);
               else ptx::tma_load_2d_pair(sa + j * (64 * 128), mapA, full_c, k0, ar);
@@ -471,6 +495,7 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               }
 #pragma unroll
               for (int j = 0; j < Sh::B_COLS / 64; ++j) {
+                if (gather) break;
                 if (CG == 1) ptx::tma_load_2d(sb + j * (BK * 128), &map_b, full_c, qb + j * 64, r0);
                 else ptx::tma_load_2d_pair(sb + j * (BK * 128), &map_b, full_c, qb + j * 64, r0);
               }
@@ -481,8 +506,36 @@ gmm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
               for (int j = 0; j < BMC / 64; ++j)
                 ptx::tma_load_2d(sa + j * (BK * 128), &map_a, rb, pa + j * 64, r0);
 #pragma unroll
-              for (int j = 0; j < Sh::B_COLS / 64; ++j)
+              for (int j = 0; j < Sh::B_COLS / 64; ++j) {
+                if (gather) break;
                 ptx::tma_load_2d(sb + j * (BK * 128), &map_b, rb, qb + j * 64, r0);
+              }
+            }
+          }
+        }
+        if (gather) {
+          // The gathered operand: every lane fetches 4 rows with one gather4 per 64-column
+          // box (its bytes are in the stage's expect_tx armed by lane 0 above).
+          __syncwarp();
+          const uint32_t sa = ptx::smem_u32(&s.a[stage][0]);
+          const uint32_t sb = ptx::smem_u32(&s.b[stage][0]);
+          const uint32_t full_local = ptx::smem_u32(&s.full[stage]);
+          const uint32_t full_c = CG == 1 ? full_local : ptx::mapa_shared(full_local, 0);
+          if (MODE != kModeWgrad) {
+            ptx::tma_gather4(sa + lane * 512, &map_a, full_c, kb * BK, grow[0], grow[1], grow[2],
+                             grow[3]);
+          } else {
+            const int r0 = ti.row0 + kb * BK;
+            const bool masked = ti.row0 + ti.rows - r0 < BK;
+            const int qb = ti.n_blk * BN + (int)rank * Sh::B_COLS;
+            const uint32_t bar = masked ? ptx::smem_u32(&s.raw[stage]) : full_c;
+            for (int j = lane >> 4; j < Sh::B_COLS / 64; j += 2) {
+              const uint32_t dst = sb + j * (BK * 128) + (lane & 15) * 512;
+              if (CG == 1 || masked)
+                ptx::tma_gather4(dst, &map_b, bar, qb + j * 64, grow[0], grow[1], grow[2], grow[3]);
+              else
+                ptx::tma_gather4_pair(dst, &map_b, bar, qb + j * 64, grow[0], grow[1], grow[2],
+                                      grow[3]);
             }
           }
         }

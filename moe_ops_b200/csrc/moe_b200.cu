@@ -196,15 +196,26 @@ struct RowsSeg2 {
   int64_t k_red;
 };
 
+// A gathered operand: row r is row rows[r] of a [src_rows, ...] tensor (TMA gather4).
+struct GatherArgs {
+  const int32_t* rows;
+  int64_t src_rows;
+};
+
 static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offsets, int plus_one,
                     int64_t m_total, int64_t n_out, int64_t k_red, int E, bool b_mn, int dtype,
                     cudaStream_t stream, const SwiGLUBwdArgs* sw = nullptr,
-                    const RowsSeg2* seg2 = nullptr) {
+                    const RowsSeg2* seg2 = nullptr, const GatherArgs* ga = nullptr) {
   if (m_total == 0 || n_out == 0) return MOE_OK;
   const bool tc = dtype != MOE_F32 && k_red % 8 == 0 && n_out % 8 == 0 && E <= gmm::kMaxGroups &&
                   aligned16(A) && aligned16(B) && aligned16(C) && m_total < (1ll << 31) &&
                   n_out < (1ll << 31) && k_red < (1ll << 31) &&
                   (!sw || (aligned16(sw->gate) && aligned16(sw->up) && aligned16(sw->grad_up)));
+  if (ga) {
+    MOE_REQUIRE(tc && k_red > 0 && !sw && !seg2 && ga->rows != nullptr && ga->src_rows > 0 &&
+                    ga->src_rows < (1ll << 31),
+                "gmm gather: needs the tensor-core path (16-bit, aligned, sizes multiples of 8)");
+  }
   if (sw && (!tc || k_red == 0)) {
     // The product into C, then the SwiGLU backward in place (each element is read before
     // the same thread writes it).
@@ -239,13 +250,14 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   }
   // Single-CTA tiles: measured on B200 against SM pairs (with half tail tiles) for 256 to
   // 2048 rows per expert at d=4096 / H=11008 shapes, they run 3-15 % faster in this mode.
-  const int cg = (sw || seg2) ? 1 : pick_cg(1);
+  const int cg = (sw || seg2 || ga) ? 1 : pick_cg(1);
   const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
-    const uint64_t dims[2] = {(uint64_t)k_red, (uint64_t)m_total};
-    // 64-row boxes: two per CTA, one per CTA of a half tile.
-    const uint32_t box[2] = {(uint32_t)gmm::BK, 64u};
+    // 64-row boxes: two per CTA, one per CTA of a half tile; a gathered A: one-row boxes
+    // over the source rows.
+    const uint64_t dims[2] = {(uint64_t)k_red, (uint64_t)(ga ? ga->src_rows : m_total)};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, ga ? 1u : 64u};
     int rc = make_map(&ma, A, dtype, 2, dims, box);
     if (rc) return rc;
   }
@@ -295,6 +307,10 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
   p.p_out = 0;
   p.k_red = (int)k_red;
   p.out = C;
+  if (ga) {
+    p.gather_rows = ga->rows;
+    p.gather_src_rows = (int)ga->src_rows;
+  }
   if (sw) {
     p.out_up = sw->grad_up;
     p.in_gate = sw->gate;
@@ -323,11 +339,16 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
 
 // Wgrad mode: Out[g] [P, Q] = X[rows of g]^T . Y[rows of g]; X [m_total, P], Y [m_total, Q].
 static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* offsets, int plus_one,
-                     int64_t m_total, int64_t P, int64_t Q, int E, int dtype, cudaStream_t stream) {
+                     int64_t m_total, int64_t P, int64_t Q, int E, int dtype, cudaStream_t stream,
+                     const GatherArgs* ga = nullptr) {
   if (P == 0 || Q == 0 || E == 0) return MOE_OK;
   const bool tc = dtype != MOE_F32 && P % 8 == 0 && Q % 8 == 0 && E <= gmm::kMaxGroups &&
                   aligned16(X) && aligned16(Y) && aligned16(Out) && m_total > 0 &&
                   m_total < (1ll << 31) && P < (1ll << 31) && Q < (1ll << 31);
+  if (ga) {
+    MOE_REQUIRE(tc && ga->rows != nullptr && ga->src_rows > 0 && ga->src_rows < (1ll << 31),
+                "gmm wgrad gather: needs the tensor-core path (16-bit, aligned, sizes multiples of 8)");
+  }
   if (!tc) {
     const dim3 grid((unsigned)((Q + simt::TN - 1) / simt::TN), (unsigned)((P + simt::TM - 1) / simt::TM),
                     (unsigned)E);
@@ -358,8 +379,9 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
     if (rc) return rc;
   }
   {
-    const uint64_t dims[2] = {(uint64_t)Q, (uint64_t)m_total};
-    const uint32_t box[2] = {64, (uint32_t)gmm::BK};
+    // A gathered Y: one-row boxes over the source rows.
+    const uint64_t dims[2] = {(uint64_t)Q, (uint64_t)(ga ? ga->src_rows : m_total)};
+    const uint32_t box[2] = {64, ga ? 1u : (uint32_t)gmm::BK};
     int rc = make_map(&my, Y, dtype, 2, dims, box);
     if (rc) return rc;
   }
@@ -382,6 +404,10 @@ static int gmm_wgrad(const void* X, const void* Y, void* Out, const int32_t* off
   {
     const char* e = getenv("MOE_B200_WGRAD_ORDER");  // tuning: p = row blocks fastest
     p.q_fastest = (e && e[0] == 'p') ? 0 : 1;
+  }
+  if (ga) {
+    p.gather_rows = ga->rows;
+    p.gather_src_rows = (int)ga->src_rows;
   }
   return launch_fmt_cg<gmm::kModeWgrad, true, true>(dtype, cg, mx, my, mo, p, stream);
 }
@@ -506,7 +532,8 @@ namespace moe {
 static int permute_impl(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
                         int32_t topk, int64_t num_cols, int32_t E, int32_t capacity,
                         int32_t row_limit, void* permuted, int32_t* row_id_map, int32_t* offsets,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+                        void* workspace, size_t workspace_bytes, void* stream,
+                        int32_t* row_src = nullptr) {
   const int64_t num_slots = num_tokens * topk;
   cudaStream_t s = (cudaStream_t)stream;
   if (num_slots == 0) {
@@ -538,7 +565,7 @@ static int permute_impl(const void* input, int dtype, const int32_t* indices, in
   }
   permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
                                                           cnt, w.num_tiles, row_id_map, offsets,
-                                                          capacity, row_limit);
+                                                          capacity, row_limit, row_src);
   MOE_LAUNCH_CHECK();
   if (num_cols == 0) return MOE_OK;
   const int es = dtype_size(dtype);
@@ -581,6 +608,18 @@ int moe_permute(const void* input, int dtype, const int32_t* indices, int64_t nu
   MOE_REQUIRE(num_slots < (1ll << 31), "permute: T*K must fit in int32");
   return permute_impl(input, dtype, indices, num_tokens, topk, num_cols, E, INT32_MAX, INT32_MAX,
                       permuted, row_id_map, offsets, workspace, workspace_bytes, stream);
+}
+
+int moe_permute_index(const int32_t* indices, int64_t num_tokens, int32_t topk, int32_t E,
+                      int32_t* row_id_map, int32_t* offsets, int32_t* row_src, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  MOE_REQUIRE(num_tokens >= 0 && topk > 0 && topk <= 32, "permute_index: bad sizes T=%lld K=%d",
+              (long long)num_tokens, topk);
+  MOE_REQUIRE(E > 0 && E <= kMaxExperts, "permute_index: need 0 < E <= %d (E=%d)", kMaxExperts, E);
+  MOE_REQUIRE(num_tokens * topk < (1ll << 31), "permute_index: T*K must fit in int32");
+  MOE_REQUIRE(row_src != nullptr, "permute_index: row_src is NULL");
+  return permute_impl(nullptr, MOE_BF16, indices, num_tokens, topk, 0, E, INT32_MAX, INT32_MAX,
+                      nullptr, row_id_map, offsets, workspace, workspace_bytes, stream, row_src);
 }
 
 int moe_permute_capacity(const void* input, int dtype, const int32_t* indices, int64_t num_tokens,
@@ -755,6 +794,35 @@ int moe_gmm_fwd(const void* A, const void* B, void* C, const int32_t* offsets, i
                   (cudaStream_t)stream);
 }
 
+int moe_gmm_fwd_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows, const void* B,
+                       void* C, const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                       int64_t n, int64_t k, int32_t E, int trans_b, int dtype, void* stream) {
+  int rc = check_gmm_args(A_src, B, C, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  if (E == 0 || m_total == 0 || n == 0) return MOE_OK;
+  const GatherArgs ga{a_rows, a_src_rows};
+  return gmm_rows(A_src, B, C, offsets, num_offsets == E + 1, m_total, n, k, E, !trans_b, dtype,
+                  (cudaStream_t)stream, nullptr, nullptr, &ga);
+}
+
+int moe_gmm_wgrad_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows,
+                         const void* grad_C, void* grad_B, const int32_t* offsets,
+                         int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t E,
+                         int trans_b, int dtype, void* stream) {
+  int rc = check_gmm_args(A_src, grad_C, grad_B, offsets, num_offsets, m_total, n, k, E, dtype);
+  if (rc) return rc;
+  MOE_REQUIRE(trans_b != 0, "gmm_wgrad_gather: supports trans_b (grad_B [E, N, K]) only");
+  if (E == 0) return MOE_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (m_total == 0) {
+    MOE_CUDA_CHECK(cudaMemsetAsync(grad_B, 0, (size_t)E * n * k * dtype_size(dtype), s));
+    return MOE_OK;
+  }
+  const GatherArgs ga{a_rows, a_src_rows};
+  return gmm_wgrad(grad_C, A_src, grad_B, offsets, num_offsets == E + 1, m_total, n, k, E, dtype, s,
+                   &ga);
+}
+
 int moe_gmm_dgrad(const void* grad_C, const void* B, void* grad_A, const int32_t* offsets,
                   int32_t num_offsets, int64_t m_total, int64_t n, int64_t k, int32_t E,
                   int trans_b, int dtype, void* stream) {
@@ -805,10 +873,12 @@ int moe_gmm_wgrad(const void* A, const void* grad_C, void* grad_B, const int32_t
   return gmm_wgrad(A, grad_C, grad_B, offsets, plus_one, m_total, k, n, E, dtype, s);
 }
 
-int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, void* gate,
-                        void* up, void* h, const int32_t* offsets, int32_t num_offsets,
-                        int64_t m_total, int64_t n, int64_t k, int32_t E, int trans_b, int dtype,
-                        void* stream) {
+}  // extern "C"
+
+static int gate_up_impl(const void* A, const void* B_gate, const void* B_up, void* gate, void* up,
+                        void* h, const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                        int64_t n, int64_t k, int32_t E, int trans_b, int dtype, void* stream,
+                        const GatherArgs* ga) {
   int rc = check_gmm_args(A, B_gate, gate, offsets, num_offsets, m_total, n, k, E, dtype);
   if (rc) return rc;
   MOE_REQUIRE((B_up && up && h) || m_total == 0 || E == 0, "gmm_gate_up: NULL operand");
@@ -819,6 +889,11 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
                   aligned16(A) && aligned16(B_gate) && aligned16(B_up) && aligned16(gate) &&
                   aligned16(up) && aligned16(h) && m_total < (1ll << 31) && n < (1ll << 31) &&
                   k < (1ll << 31);
+  if (ga) {
+    MOE_REQUIRE(tc && ga->rows != nullptr && ga->src_rows > 0 && ga->src_rows < (1ll << 31),
+                "gmm_gate_up gather: needs the tensor-core path (16-bit, aligned, sizes multiples "
+                "of 8)");
+  }
   if (!tc) {
     // Same results from the separate kernels: two grouped GEMMs, then the SwiGLU pass.
     rc = gmm_rows(A, B_gate, gate, offsets, plus_one, m_total, n, k, E, !trans_b, dtype, s);
@@ -829,8 +904,8 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
   }
   CUtensorMap maps[6];  // A, B_gate, h, B_up, gate, up
   {
-    const uint64_t dims[2] = {(uint64_t)k, (uint64_t)m_total};
-    const uint32_t box[2] = {(uint32_t)gmm::BK, 64u};
+    const uint64_t dims[2] = {(uint64_t)k, (uint64_t)(ga ? ga->src_rows : m_total)};
+    const uint32_t box[2] = {(uint32_t)gmm::BK, ga ? 1u : 64u};
     if ((rc = make_map(&maps[0], A, dtype, 2, dims, box))) return rc;
   }
   for (int i = 0; i < 2; ++i) {
@@ -864,6 +939,10 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
   p.out = h;
   p.out_gate = gate;
   p.out_up = up;
+  if (ga) {
+    p.gather_rows = ga->rows;
+    p.gather_src_rows = (int)ga->src_rows;
+  }
   const CUtensorMap* extra = &maps[3];
   if (dtype == MOE_BF16)
     return trans_b ? launch_sm100<gmm::kModeGateUp, 1, 1, false, false, __nv_bfloat16>(
@@ -874,6 +953,26 @@ int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, voi
                                                                              maps[2], p, s, extra)
                  : launch_sm100<gmm::kModeGateUp, 1, 0, false, true, __half>(maps[0], maps[1],
                                                                             maps[2], p, s, extra);
+}
+
+extern "C" {
+
+int moe_gmm_gate_up_fwd(const void* A, const void* B_gate, const void* B_up, void* gate,
+                        void* up, void* h, const int32_t* offsets, int32_t num_offsets,
+                        int64_t m_total, int64_t n, int64_t k, int32_t E, int trans_b, int dtype,
+                        void* stream) {
+  return gate_up_impl(A, B_gate, B_up, gate, up, h, offsets, num_offsets, m_total, n, k, E, trans_b,
+                      dtype, stream, nullptr);
+}
+
+int moe_gmm_gate_up_fwd_gather(const void* A_src, const int32_t* a_rows, int64_t a_src_rows,
+                               const void* B_gate, const void* B_up, void* gate, void* up, void* h,
+                               const int32_t* offsets, int32_t num_offsets, int64_t m_total,
+                               int64_t n, int64_t k, int32_t E, int trans_b, int dtype,
+                               void* stream) {
+  const GatherArgs ga{a_rows, a_src_rows};
+  return gate_up_impl(A_src, B_gate, B_up, gate, up, h, offsets, num_offsets, m_total, n, k, E,
+                      trans_b, dtype, stream, &ga);
 }
 
 int moe_gmm_dgrad_swiglu_bwd(const void* grad_C, const void* B, const void* gate, const void* up,

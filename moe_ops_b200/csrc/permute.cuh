@@ -59,13 +59,14 @@ permute_hist_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int E,
 // Capacity (dropping): a slot whose stable rank inside its expert is >= `capacity`, or
 // whose destination row would be >= `row_limit`, is dropped: row_id_map = -1 and no row.
 // The offsets count the kept rows only, so the grouped GEMMs never see a dropped slot.
-// Both limits at INT32_MAX give the plain permute.
+// Both limits at INT32_MAX give the plain permute.  `row_src` (nullable) receives the
+// inverse map: row_src[row] = the token whose slot lands in that row.
 // Dynamic shared memory: (kPermTileWarps + 3) * E int32.
 __global__ void __launch_bounds__(kPermTile)
 permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t num_tokens,
                     int K, int E, const int32_t* __restrict__ cnt, int64_t num_tiles,
                     int32_t* __restrict__ row_id_map, int32_t* __restrict__ offsets,
-                    int32_t capacity, int32_t row_limit) {
+                    int32_t capacity, int32_t row_limit, int32_t* __restrict__ row_src) {
   extern __shared__ int32_t s_cnt[];     // [kPermTileWarps][E]
   int32_t* s_before = s_cnt + kPermTileWarps * E;  // [E] this expert's rows in earlier tiles
   int32_t* s_total = s_before + E;                 // [E] this expert's rows in all tiles
@@ -139,6 +140,7 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
       if (r < capacity && s_first[e] + r < row_limit) dst = s_first[e] + r;
     }
     row_id_map[k * num_tokens + t] = dst;
+    if (row_src != nullptr && dst >= 0) row_src[dst] = (int32_t)t;  // inverse map: row -> token
   }
 }
 

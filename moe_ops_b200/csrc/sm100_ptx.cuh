@@ -155,6 +155,29 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(cbar)
       : "memory");
 }
+// Four rows of a 2-D tensor map whose box is one row high: rows r0..r3 (any order, any
+// values inside the tensor), columns c0.. of the box width, land as four consecutive box
+// rows at dst (the map's swizzle applies as for a tiled load of four rows there).
+__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t c0, int32_t r0, int32_t r1, int32_t r2,
+                                            int32_t r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(bar)
+      : "memory");
+}
+// tma_gather4 for a CTA pair: completes its bytes on an mbarrier that may sit in the other
+// CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t cbar, int32_t c0, int32_t r0,
+                                                 int32_t r1, int32_t r2, int32_t r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(cbar)
+      : "memory");
+}
 // Shared -> global tensor stores, completed through bulk groups of the issuing thread.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0,
                                              int32_t c1) {

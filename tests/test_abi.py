@@ -102,7 +102,7 @@ def test_every_custom_op_has_a_fake_impl():
 
     from torch._subclasses.fake_tensor import FakeTensorMode
     import moe_ops_b200  # noqa: F401  (registers the ops)
-    from moe_ops_b200 import gate_up_ops, swiglu_ops  # noqa: F401
+    from moe_ops_b200 import fused_permute_ops, gate_up_ops, swiglu_ops  # noqa: F401
 
     bf = torch.bfloat16
     ops = torch.ops.moeb200
@@ -130,6 +130,12 @@ def test_every_custom_op_has_a_fake_impl():
             "permute_countsort": (ops.permute_countsort(x, idx, 0, E),
                                   [((T * K, d), bf), ((T * K,), torch.int32), ((E + 1,), torch.int32)]),
             "scatter_rows": (ops.scatter_rows(x, rid, T * K, K), [((T * K, d), bf)]),
+            "permute_index": (ops.permute_index(idx, E),
+                              [((T * K,), torch.int32), ((E + 1,), torch.int32), ((T * K,), torch.int32)]),
+            "gmm_gate_up_fwd_gather_raw": (ops.gmm_gate_up_fwd_gather_raw(x, rid, Wgu, Wgu, off),
+                                           [((T * K, H), bf)] * 3),
+            "gmm_wgrad_gather_raw": (ops.gmm_wgrad_gather_raw(x, rid, gate, off, E),
+                                     [((E, H, d), bf)]),
             "permute_capacity": (ops.permute_capacity(x, idx, E, 5, 0),
                                  [((E * 5, d), bf), ((T * K,), torch.int32), ((E + 1,), torch.int32)]),
             "unpermute_forward": (ops.unpermute_forward(A, rid, prob, T, K), [((T, d), bf)]),
