@@ -309,6 +309,7 @@ def run_ours(args):
         with torch.no_grad():
             for w in (layer.w_gate, layer.w_up, layer.w_down):
                 w.normal_(0.0, 0.02, generator=gen)
+        layer.fused_permute = args.fused_permute
     else:
         # Expert parallelism: this rank holds E/world experts, the router is replicated.
         from moe_ops_b200.ep import EPMoELayer
@@ -551,6 +552,7 @@ def run_ours(args):
             "parallelism": ep_label,
             "ep_transport": args.ep_transport if world > 1 else None,
             "tokens_per_rank": T,
+            "fused_permute": bool(args.fused_permute) if world == 1 else None,
             "l2": "inputs larger than L2 (expert weights 17.3 GB cfg4 / 22.5 GB cfg5 in total), "
                   "no flush",
             "gemm_flops_per_step": flops_step * world,
@@ -877,6 +879,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-ops", action="store_true", help="N = 1: leave out the per-op block")
+    ap.add_argument("--fused-permute", action="store_true",
+                    help="N = 1: the expert GEMMs gather their rows from x (no permuted copy)")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="time the step as a replayed CUDA graph (auto: N > 1 on the peer-memory "
                          "transport, where the host's per-launch work would otherwise pace the "
