@@ -46,6 +46,15 @@ int num_sms(int device);
 // Codes: 1 = bounded wait gave up (GEMM pipeline), 2 = expert index out of range.
 __device__ int g_device_error;
 
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel of the stream still runs; pdl_wait() blocks until that
+// kernel has completed and its memory is visible (a no-op for an ordinary launch).
+// pdl_launch_dependents() lets the next kernel of the stream start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void raise_device_error(int code) {
   atomicCAS(&g_device_error, 0, code);
 }

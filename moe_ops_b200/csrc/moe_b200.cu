@@ -155,6 +155,25 @@ static int launch_sm100(const CUtensorMap& ma, const CUtensorMap& mb, const CUte
   return MOE_OK;
 }
 
+// Launch with programmatic stream serialization: the kernel may start before the previous
+// kernel of the stream completes and waits for it with pdl_wait() (hides launch latency in
+// chains of short kernels).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // CTA-group choice: MOE_B200_GMM_CG=1|2 forces it (tuning/tests); otherwise `auto_cg`.
@@ -563,10 +582,9 @@ static int permute_impl(const void* input, int dtype, const int32_t* indices, in
       if (dev < 64) rank_smem_set[dev] = rank_smem;
     }
   }
-  permute_rank_kernel<<<tiles, kPermTile, rank_smem, s>>>(indices, num_slots, num_tokens, topk, E,
-                                                          cnt, w.num_tiles, row_id_map, offsets,
-                                                          capacity, row_limit, row_src);
-  MOE_LAUNCH_CHECK();
+  MOE_CUDA_CHECK(launch_pdl(permute_rank_kernel, dim3(tiles), dim3(kPermTile), rank_smem, s, indices,
+                            num_slots, num_tokens, topk, E, (const int32_t*)cnt, w.num_tiles,
+                            row_id_map, offsets, capacity, row_limit, row_src));
   if (num_cols == 0) return MOE_OK;
   const int es = dtype_size(dtype);
   const bool vec = (num_cols * es) % 16 == 0 && aligned16(input) && aligned16(permuted);
@@ -575,11 +593,13 @@ static int permute_impl(const void* input, int dtype, const int32_t* indices, in
   {                                                                                                 \
     const LocalRows<TT> rows{(TT*)permuted, row_id_map, num_tokens, num_cols};                      \
     if (vec)                                                                                        \
-      permute_copy_kernel<TT, true><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,          \
-                                                                    num_tokens, topk, num_cols);   \
+      MOE_CUDA_CHECK(launch_pdl(permute_copy_kernel<TT, true, LocalRows<TT>>, grid,                 \
+                                dim3(kRowWarps * 32), 0, s, (const TT*)input, rows, num_tokens,     \
+                                topk, num_cols));                                                  \
     else                                                                                            \
-      permute_copy_kernel<TT, false><<<grid, kRowWarps * 32, 0, s>>>((const TT*)input, rows,         \
-                                                                     num_tokens, topk, num_cols);  \
+      MOE_CUDA_CHECK(launch_pdl(permute_copy_kernel<TT, false, LocalRows<TT>>, grid,                \
+                                dim3(kRowWarps * 32), 0, s, (const TT*)input, rows, num_tokens,     \
+                                topk, num_cols));                                                  \
   }
   switch (dtype) {
     case MOE_F32: MOE_COPY(float) break;
@@ -587,7 +607,6 @@ static int permute_impl(const void* input, int dtype, const int32_t* indices, in
     default: MOE_COPY(__nv_bfloat16) break;
   }
 #undef MOE_COPY
-  MOE_LAUNCH_CHECK();
   return MOE_OK;
 }
 }  // namespace moe

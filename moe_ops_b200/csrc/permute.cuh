@@ -36,6 +36,7 @@ inline int64_t permute_num_tiles(int64_t num_slots) {
 __global__ void __launch_bounds__(kPermTile)
 permute_hist_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int E,
                     int32_t* __restrict__ cnt, int64_t num_tiles) {
+  pdl_launch_dependents();
   extern __shared__ int32_t s_hist[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) s_hist[e] = 0;
   __syncthreads();
@@ -67,6 +68,8 @@ permute_rank_kernel(const int32_t* __restrict__ flat, int64_t num_slots, int64_t
                     int K, int E, const int32_t* __restrict__ cnt, int64_t num_tiles,
                     int32_t* __restrict__ row_id_map, int32_t* __restrict__ offsets,
                     int32_t capacity, int32_t row_limit, int32_t* __restrict__ row_src) {
+  pdl_launch_dependents();
+  pdl_wait();  // the histogram counts
   extern __shared__ int32_t s_cnt[];     // [kPermTileWarps][E]
   int32_t* s_before = s_cnt + kPermTileWarps * E;  // [E] this expert's rows in earlier tiles
   int32_t* s_total = s_before + E;                 // [E] this expert's rows in all tiles
@@ -228,11 +231,24 @@ struct PeerRows {
 };
 
 // ---------------------------------------------------------------- 4. copy (token-major)
+// 16-byte chunks each lane keeps in flight in the row kernels (measured on B200, cfg3 rows of
+// 8 KB: permute copy 4 -> 16 took permute from 71 % to 74 % of the copy bandwidth; unpermute
+// 2 -> 4 from 79 % to 87 %, unpermute backward 2 -> 4 from 79 % to 88 %).
+#ifndef MOE_PERMUTE_COPY_U
+#define MOE_PERMUTE_COPY_U 16
+#endif
+#ifndef MOE_UNPERMUTE_U
+#define MOE_UNPERMUTE_U 4
+#endif
+#ifndef MOE_UNPERMUTE_BWD_U
+#define MOE_UNPERMUTE_BWD_U 4
+#endif
 // VEC: rows are 16-byte multiples and 16-byte aligned (uint4 path), else element path.
 template <typename T, bool VEC, class Rows>
 __global__ void __launch_bounds__(kRowWarps * 32)
 permute_copy_kernel(const T* __restrict__ input, Rows dst_rows, int64_t num_tokens, int K,
                     int64_t num_cols) {
+  pdl_wait();  // row_id_map
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
   if (t >= num_tokens) return;
@@ -245,7 +261,8 @@ permute_copy_kernel(const T* __restrict__ input, Rows dst_rows, int64_t num_toke
   if constexpr (VEC) {
     const int64_t nv = num_cols / Vec16<T>::N;
     const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    constexpr int U = 4;
+    // U 16-byte chunks per lane in flight: a warp holds U * 512 bytes of its row.
+    constexpr int U = MOE_PERMUTE_COPY_U;
     for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
       uint4 v[U];
 #pragma unroll
@@ -303,7 +320,7 @@ unpermute_fwd_kernel(Rows src_rows, const P* __restrict__ prob, T* __restrict__ 
   if constexpr (VEC) {
     constexpr int NV = Vec16<T>::N;
     const int64_t nv = num_cols / NV;
-    constexpr int U = 2;
+    constexpr int U = MOE_UNPERMUTE_U;
     for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
       float acc[U][NV];
 #pragma unroll
@@ -394,7 +411,7 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, RowsIn in_rows, RowsOut act
   if constexpr (VEC) {
     // U 16-byte chunks per lane and iteration: all their loads are issued before use.
     constexpr int NV = Vec16<T>::N;
-    constexpr int U = 2;
+    constexpr int U = MOE_UNPERMUTE_BWD_U;
     const int64_t nv = num_cols / NV;
     for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
       uint4 graw[U];
