@@ -267,9 +267,9 @@ static int gmm_rows(const void* A, const void* B, void* C, const int32_t* offset
     MOE_LAUNCH_CHECK();
     return MOE_OK;
   }
-  // Single-CTA tiles: measured on B200 against SM pairs (with half tail tiles) for 256 to
-  // 2048 rows per expert at d=4096 / H=11008 shapes, they run 3-15 % faster in this mode.
-  const int cg = (sw || seg2 || ga) ? 1 : pick_cg(1);
+  // SM pairs once experts average 1024 rows or more (measured, cfg2 d=4096: dgrad 1290 vs
+  // 1237 TFLOP/s, forward even); single CTAs below (cfg4's 256 rows: forward 956 vs 916).
+  const int cg = (sw || seg2 || ga) ? 1 : pick_cg(m_total >= 1024ll * E ? 2 : 1);
   const uint32_t b_cols = (uint32_t)(gmm::BN / cg);
   CUtensorMap ma, mb;
   {
