@@ -674,6 +674,11 @@ def ops_block(dev, steps=20, warmup=3):
                "torch_grouped_mm_dgrad": lambda: torch.nn.functional.grouped_mm(gC, B, offs=ends)}
         if tg is not None:
             fns["reference_triton_fwd"] = lambda: tg.grouped_gemm(A, B, off, trans_b=True)
+            # its grad_A GEMM (the TMA forward on a transposed weight copy, as its autograd
+            # backward runs it, grouped_gemm_ops_sm90.py:228-231) and its weight gradient
+            fns["reference_triton_dgrad"] = lambda: torch.ops.tg.gmm_tma_fwd_raw(
+                gC, B.transpose(1, 2).contiguous(), off, trans_b=False)
+            fns["reference_triton_wgrad"] = lambda: torch.ops.tg.gmm_bwd_B_raw(A, B, off, gC, True)
         for k, fn in fns.items():
             try:
                 ms = _time_events(fn, steps, warmup)
@@ -686,18 +691,26 @@ def ops_block(dev, steps=20, warmup=3):
     if tg is None:
         res["reference_triton"] = f"not timed: {why}"
     else:
-        res["reference_triton"] = "triton_gmm_ops.grouped_gemm forward (its sm90+ TMA path, " \
-                                  "autotuned on first call) from baseline/_ref, unchanged"
+        res["reference_triton"] = "triton_gmm_ops from baseline/_ref, unchanged: grouped_gemm " \
+                                  "forward (its sm90+ TMA path, autotuned on first call), its " \
+                                  "dgrad as its backward runs it (weight transpose copy + TMA " \
+                                  "forward) and its wgrad kernel (tg::gmm_bwd_B_raw)"
     del A, B, gC
     res["cfg3_routing"] = _routing_ops(dev, steps=max(steps, 50), warmup=warmup)
+    if tg is not None:
+        res["cfg3_routing_reference_triton"] = _routing_ops(dev, steps=max(steps, 50),
+                                                            warmup=warmup, impl=tg)
     return res
 
 
-def _routing_ops(dev, steps, warmup):
+def _routing_ops(dev, steps, warmup, impl=None):
     """BASELINE config 3 routing primitives (T=8192, d=4096 bf16, E=64, K=2), each captured
     in a CUDA graph and replayed (GPU time only); GB/s of unique bytes and the fraction of
-    the measured HBM copy bandwidth."""
-    import moe_ops_b200 as M
+    the measured HBM copy bandwidth.  impl: a module with the reference's API (its own
+    Triton kernels, from baseline/_ref) in place of this library."""
+    import moe_ops_b200
+
+    M = impl or moe_ops_b200
 
     peaks, _ = _peaks()
     g = torch.Generator(device=dev).manual_seed(1)
@@ -718,13 +731,18 @@ def _routing_ops(dev, steps, warmup):
     }
     res = {}
     for name, (fn, nbytes) in cases.items():
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            fn()
-        ms = _time_events(graph.replay, steps, warmup)
+        try:
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            ms = _time_events(graph.replay, steps, warmup)
+        except Exception as e:  # noqa: BLE001  (a reference op that cannot run or be captured)
+            torch.cuda.synchronize()
+            res[name] = {"error": f"{type(e).__name__}: {e}"[:120]}
+            continue
         gbs = nbytes / (ms * 1e-3) / 1e9
         res[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
                      "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4), "bytes": nbytes}

@@ -233,12 +233,12 @@ struct PeerRows {
 // ---------------------------------------------------------------- 4. copy (token-major)
 // 16-byte chunks each lane keeps in flight in the row kernels (measured on B200, cfg3 rows of
 // 8 KB: permute copy 4 -> 16 took permute from 71 % to 74 % of the copy bandwidth; unpermute
-// 2 -> 4 from 79 % to 87 %, unpermute backward 2 -> 4 from 79 % to 88 %).
+// 2 -> 8 from 79 % to 88 %, unpermute backward 2 -> 4 from 79 % to 88 %).
 #ifndef MOE_PERMUTE_COPY_U
 #define MOE_PERMUTE_COPY_U 16
 #endif
 #ifndef MOE_UNPERMUTE_U
-#define MOE_UNPERMUTE_U 4
+#define MOE_UNPERMUTE_U 8
 #endif
 #ifndef MOE_UNPERMUTE_BWD_U
 #define MOE_UNPERMUTE_BWD_U 4
