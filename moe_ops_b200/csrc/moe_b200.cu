@@ -174,6 +174,27 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// The unpermute-forward kernel for a row set R: the vector path instantiated for the
+// smallest KMAX >= topk (all K slots' loads in flight together), the element path once.
+#define MOE_UNP_LAUNCH(TT, PP, R)                                                                   \
+  if (vec) {                                                                                        \
+    if (topk <= 2)                                                                                  \
+      unpermute_fwd_kernel<TT, PP, 2, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
+          R, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+    else if (topk <= 4)                                                                             \
+      unpermute_fwd_kernel<TT, PP, 4, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
+          R, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+    else if (topk <= 8)                                                                             \
+      unpermute_fwd_kernel<TT, PP, 8, true><<<grid, kRowWarps * 32, 0, s>>>(                        \
+          R, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+    else                                                                                            \
+      unpermute_fwd_kernel<TT, PP, 32, true><<<grid, kRowWarps * 32, 0, s>>>(                       \
+          R, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+  } else {                                                                                          \
+    unpermute_fwd_kernel<TT, PP, 32, false><<<grid, kRowWarps * 32, 0, s>>>(                        \
+        R, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                  \
+  }
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // CTA-group choice: MOE_B200_GMM_CG=1|2 forces it (tuning/tests); otherwise `auto_cg`.
@@ -728,12 +749,7 @@ int moe_unpermute_fwd(const void* input, int dtype, const int32_t* row_id_map, c
 #define MOE_UNP(TT, PP)                                                                              \
   {                                                                                                 \
     const LocalRows<const TT> rows{(const TT*)input, row_id_map, num_tokens, num_cols};             \
-    if (vec)                                                                                        \
-      unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                            \
-          rows, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                             \
-    else                                                                                            \
-      unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                           \
-          rows, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                             \
+    MOE_UNP_LAUNCH(TT, PP, rows)                                                                    \
   }
 #define MOE_UNP_P(TT)                                                                                \
   switch (pd) {                                                                                     \
@@ -1173,12 +1189,7 @@ int moe_ep_combine(const void* const* bases, int dtype, const int32_t* ranks, co
 #define MOE_EPC(TT, PP)                                                                              \
   {                                                                                                 \
     const PeerRows<const TT> r{(const TT* const*)bases, ranks, rows, num_tokens, num_cols, status};  \
-    if (vec)                                                                                        \
-      unpermute_fwd_kernel<TT, PP, true><<<grid, kRowWarps * 32, 0, s>>>(                            \
-          r, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
-    else                                                                                            \
-      unpermute_fwd_kernel<TT, PP, false><<<grid, kRowWarps * 32, 0, s>>>(                           \
-          r, (const PP*)prob, (TT*)out, num_tokens, topk, num_cols);                                \
+    MOE_UNP_LAUNCH(TT, PP, r)                                                                       \
   }
 #define MOE_EPC_P(TT)                                                                                \
   switch (pd) {                                                                                     \

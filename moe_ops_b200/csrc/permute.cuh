@@ -231,17 +231,19 @@ struct PeerRows {
 };
 
 // ---------------------------------------------------------------- 4. copy (token-major)
-// 16-byte chunks each lane keeps in flight in the row kernels (measured on B200, cfg3 rows of
-// 8 KB: permute copy 4 -> 16 took permute from 71 % to 74 % of the copy bandwidth; unpermute
-// 2 -> 8 from 79 % to 88 %, unpermute backward 2 -> 4 from 79 % to 88 %).
+// 16-byte loads each lane keeps in flight in the row kernels (measured on B200, cfg3 rows of
+// 8 KB, K = 2, against the HBM copy bandwidth): the permute copy holds 16 chunks of its
+// token's row (71 % -> 75 % with the launch changes); the unpermute kernels issue the loads
+// of all K slots of a column block before using the first (8 loads: forward 79 % -> 94 %;
+// 16 loads with the output-gradient chunks: backward 79 % -> 89.5 %).
 #ifndef MOE_PERMUTE_COPY_U
 #define MOE_PERMUTE_COPY_U 16
 #endif
-#ifndef MOE_UNPERMUTE_U
-#define MOE_UNPERMUTE_U 8
+#ifndef MOE_UNPERMUTE_LOADS
+#define MOE_UNPERMUTE_LOADS 8
 #endif
-#ifndef MOE_UNPERMUTE_BWD_U
-#define MOE_UNPERMUTE_BWD_U 4
+#ifndef MOE_UNPERMUTE_BWD_LOADS
+#define MOE_UNPERMUTE_BWD_LOADS 16
 #endif
 // VEC: rows are 16-byte multiples and 16-byte aligned (uint4 path), else element path.
 template <typename T, bool VEC, class Rows>
@@ -302,7 +304,9 @@ permute_copy_kernel(const T* __restrict__ input, Rows dst_rows, int64_t num_toke
 // Accumulation: acc = 0; acc = rn(acc + rn(v * p)) for k = 0..K-1 (no FMA contraction),
 // which is the rounding sequence of the reference's PyTorch oracle
 // (tests/test_unpermute.py:25-35).  A slot with row -1 contributes nothing.
-template <typename T, typename P, bool VEC, class Rows>
+// KMAX >= K: the K slots' loads of a column block are all issued before the first is used
+// (KMAX * U 16-byte loads in flight per lane), then summed in k order.
+template <typename T, typename P, int KMAX, bool VEC, class Rows>
 __global__ void __launch_bounds__(kRowWarps * 32)
 unpermute_fwd_kernel(Rows src_rows, const P* __restrict__ prob, T* __restrict__ out,
                      int64_t num_tokens, int K, int64_t num_cols) {
@@ -320,31 +324,43 @@ unpermute_fwd_kernel(Rows src_rows, const P* __restrict__ prob, T* __restrict__ 
   if constexpr (VEC) {
     constexpr int NV = Vec16<T>::N;
     const int64_t nv = num_cols / NV;
-    constexpr int U = MOE_UNPERMUTE_U;
+    constexpr int U = KMAX >= MOE_UNPERMUTE_LOADS ? 1 : MOE_UNPERMUTE_LOADS / KMAX;
+    int32_t s_k[KMAX];
+    int32_t rk_k[KMAX];
+    float p_k[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      s_k[k] = __shfl_sync(0xffffffffu, src_lane, k);
+      rk_k[k] = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
+      p_k[k] = __shfl_sync(0xffffffffu, p_lane, k);
+      if (k >= K) s_k[k] = -1;
+    }
     for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
+      uint4 raw[KMAX][U];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        if (s_k[k] < 0) continue;
+        const uint4* s4 = reinterpret_cast<const uint4*>(src_rows.at(rk_k[k], s_k[k]));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + u * 32 + lane;
+          if (c < nv) raw[k][u] = ld_stream(s4 + c);
+        }
+      }
       float acc[U][NV];
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
         for (int i = 0; i < NV; ++i) acc[u][i] = 0.f;
-      for (int k = 0; k < K; ++k) {
-        const int32_t s = __shfl_sync(0xffffffffu, src_lane, k);
-        const int32_t rk = Rows::kPeer ? __shfl_sync(0xffffffffu, rank_lane, k) : 0;
-        const float p = __shfl_sync(0xffffffffu, p_lane, k);
-        if (s < 0) continue;
-        const uint4* s4 = reinterpret_cast<const uint4*>(src_rows.at(rk, s));
-        uint4 raw[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t c = c0 + u * 32 + lane;
-          if (c < nv) raw[u] = ld_stream(s4 + c);
-        }
+      for (int k = 0; k < KMAX; ++k) {
+        if (s_k[k] < 0) continue;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           float f[NV];
-          unpack16<T>(raw[u], f);
+          unpack16<T>(raw[k][u], f);
 #pragma unroll
-          for (int i = 0; i < NV; ++i) acc[u][i] = __fadd_rn(acc[u][i], __fmul_rn(f[i], p));
+          for (int i = 0; i < NV; ++i) acc[u][i] = __fadd_rn(acc[u][i], __fmul_rn(f[i], p_k[k]));
         }
       }
       uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -411,7 +427,7 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, RowsIn in_rows, RowsOut act
   if constexpr (VEC) {
     // U 16-byte chunks per lane and iteration: all their loads are issued before use.
     constexpr int NV = Vec16<T>::N;
-    constexpr int U = MOE_UNPERMUTE_BWD_U;
+    constexpr int U = KMAX >= MOE_UNPERMUTE_BWD_LOADS ? 1 : MOE_UNPERMUTE_BWD_LOADS / KMAX;
     const int64_t nv = num_cols / NV;
     for (int64_t c0 = 0; c0 < nv; c0 += 32 * U) {
       uint4 graw[U];
@@ -420,6 +436,19 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, RowsIn in_rows, RowsOut act
         const int64_t c = c0 + u * 32 + lane;
         if (c < nv) graw[u] = ld_stream(reinterpret_cast<const uint4*>(g_row) + c);
       }
+      // every slot's rows of this column block in flight before the first is used
+      uint4 vraw[KMAX][U];
+#pragma unroll
+      for (int k = 0; k < KMAX; ++k) {
+        if (k >= K || src_k[k] < 0) continue;
+        const int32_t rk = RowsIn::kPeer ? rank_k[RowsIn::kPeer ? k : 0] : 0;
+        const uint4* in4 = reinterpret_cast<const uint4*>(in_rows.at(rk, src_k[k]));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t c = c0 + u * 32 + lane;
+          if (c < nv) vraw[k][u] = ld_stream(in4 + c);
+        }
+      }
 #pragma unroll
       for (int k = 0; k < KMAX; ++k) {
         if (k >= K) break;
@@ -427,21 +456,14 @@ unpermute_bwd_kernel(const T* __restrict__ grad_out, RowsIn in_rows, RowsOut act
         const float p = p_k[k];
         if (s < 0) continue;
         const int32_t rk = RowsIn::kPeer ? rank_k[RowsIn::kPeer ? k : 0] : 0;
-        const uint4* in4 = reinterpret_cast<const uint4*>(in_rows.at(rk, s));
         uint4* ag4 = reinterpret_cast<uint4*>(act_rows.at(rk, s));
-        uint4 vraw[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-          const int64_t c = c0 + u * 32 + lane;
-          if (c < nv) vraw[u] = ld_stream(in4 + c);
-        }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int64_t c = c0 + u * 32 + lane;
           if (c >= nv) continue;
           float g[NV], v[NV], ag[NV];
           unpack16<T>(graw[u], g);
-          unpack16<T>(vraw[u], v);
+          unpack16<T>(vraw[k][u], v);
 #pragma unroll
           for (int i = 0; i < NV; ++i) {
             dot[k] = fmaf(g[i], v[i], dot[k]);
