@@ -9,7 +9,7 @@ Per layer step (rank r of W, El = E / W local experts):
 
     forward   permute index pass (no copy) -> counts exchange (peer stores + B0)
               -> delta / offsets (tiny tensor ops) -> slot map
-              -> B1 -> dispatch: rows straight into the owners' receive buffers
+              -> dispatch: rows straight into the owners' receive buffers
               -> B2 -> gate/up + SwiGLU, down GEMMs into this rank's `down` buffer
               -> B3 -> combine: out[t] = sum_k w[t,k] * down row read from its owner
     backward  combine backward: w-scaled gradient rows pushed into the owners' `gdown`,
@@ -19,7 +19,8 @@ Per layer step (rank r of W, El = E / W local experts):
 
 The barriers Bi are device-side (``moe_ep_barrier``). Waits are bounded, and every buffer
 reuse across ranks is ordered by one of them. For example, a rank's next dispatch into a
-peer's receive buffer waits at B1 until that peer's backward has finished reading it.
+peer's receive buffer waits at B0 (the counts exchange of that step) until that peer's
+previous backward has finished reading it.
 Nothing in a step synchronises with the host or calls a collective library, and the
 barriers keep their epochs on the device, so a whole training step (forward and backward)
 can be captured in a CUDA graph and replayed.
@@ -266,7 +267,9 @@ class _PeerExperts(torch.autograd.Function):
                                        El, W, tr.capacity, _lib.ptr(ranks), _lib.ptr(rows), stream),
                    "moe_ep_slot_map")
         dt = _lib.dtype_code(x.dtype)
-        tr.barrier()                                               # B1
+        # No barrier before the dispatch: B0 (inside all_gather_counts) already waits for
+        # every peer to have reached this step, so its previous backward has finished
+        # reading the receive buffer this dispatch writes.
         _lib.check(lib.moe_ep_dispatch(_lib.ptr(x), dt, _lib.ptr(tr.bases["recv"]), _lib.ptr(ranks),
                                        _lib.ptr(rows), T, K, d, _lib.ptr(status), stream),
                    "moe_ep_dispatch")
