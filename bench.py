@@ -380,7 +380,21 @@ def run_ours(args):
     ms_total = ev0.elapsed_time(ev1)
     launches = _lib.launch_count - launches0
     timing, _lib.gemm_timing = _lib.gemm_timing, None
-    gemm_ms = sum(t[1].elapsed_time(t[2]) for t in timing)
+    # GEMM time = the union of the launches' [start, end] intervals (launches on two streams
+    # may overlap; a plain sum would count the overlap twice).
+    if timing:
+        ref_ev = timing[0][1]
+        spans = sorted((ref_ev.elapsed_time(t[1]), ref_ev.elapsed_time(t[2])) for t in timing)
+        gemm_ms, cur_a, cur_b = 0.0, spans[0][0], spans[0][1]
+        for a_, b_ in spans[1:]:
+            if a_ > cur_b:
+                gemm_ms += cur_b - cur_a
+                cur_a, cur_b = a_, b_
+            else:
+                cur_b = max(cur_b, b_)
+        gemm_ms += cur_b - cur_a
+    else:
+        gemm_ms = 0.0
     # The grouped GEMMs' FLOPs from the rows the experts actually computed on: T*K on one
     # GPU; under EP the rows this rank received (the peer transport's GEMM calls are sized
     # for its worst-case buffers, so their nominal row counts would overstate the work).
@@ -594,8 +608,8 @@ def run_ours(args):
             "eager_clocks": eager_clocks if use_graph else None,
             "gemm_time_vs_roofline": round(t_roof * 1e3 / gemm_ms, 4) if gemm_ms else None,
             "roofline_note": "achieved = 9 GEMMs x 2*rows*d*H over the rows the experts computed "
-                             "on (rank 0's, live_rows_per_rank[0]) / rank 0's summed GEMM launch "
-                             "time (CUDA events); gemm_time_vs_roofline = sum over launches of "
+                             "on (rank 0's, live_rows_per_rank[0]) / rank 0's GEMM time (the union "
+                             "of the launches' CUDA-event intervals); gemm_time_vs_roofline = sum over launches of "
                              "max(FLOP/tensor peak, DRAM bytes/copy BW, written bytes/"
                              f"{write_gbs:.0f} GB/s write BW measured in this run) / GEMM time",
             "traffic": traffic.get("bytes_per_launch") if traffic else None,

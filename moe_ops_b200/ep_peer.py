@@ -291,7 +291,8 @@ class _PeerExperts(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_out):
-        from .gate_up_ops import dgrad_dual_into, dgrad_dual_ok, gmm_dgrad_swiglu_bwd_raw
+        from .gate_up_ops import (dgrad_dual_into, dgrad_dual_ok, gmm_dgrad_swiglu_bwd_raw,
+                                  run_on_side)
         from .grouped_gemm_ops import _gmm_call, gmm_bwd_B_raw, gmm_dgrad_raw
 
         w, ranks, rows, off_local, gate, up, h, w_gate, w_up, w_down = ctx.saved_tensors
@@ -318,7 +319,9 @@ class _PeerExperts(torch.autograd.Function):
         tr.barrier()                                               # B4
         recv, gdown, dgrad = tr.buffers["recv"], tr.buffers["gdown"], tr.buffers["dgrad"]
         dgate, dup = gmm_dgrad_swiglu_bwd_raw(gdown, w_down, gate, up, off_local, True)
-        g_down = gmm_bwd_B_raw(h, w_down, off_local, gdown, True)
+        # the down projection's weight gradient needs none of the GEMMs below: a side stream
+        g_down, join = run_on_side(lambda: gmm_bwd_B_raw(h, w_down, off_local, gdown, True),
+                                   grad_out.device)
         if dgrad_dual_ok(dgate, w_gate, dup, w_up):
             dgrad_dual_into(dgate, w_gate, dup, w_up, dgrad, off_local, tr.capacity, True)
         else:
@@ -330,6 +333,7 @@ class _PeerExperts(torch.autograd.Function):
                        "moe_add_rows")
         g_gate = gmm_bwd_B_raw(recv, w_gate, off_local, dgate, True)
         g_up = gmm_bwd_B_raw(recv, w_up, off_local, dup, True)
+        join()
         tr.barrier()                                               # B5
         grad_x = torch.empty(T, d, device=grad_out.device, dtype=grad_out.dtype)
         _lib.check(lib.moe_ep_combine(_lib.ptr(tr.bases["dgrad"]), dt, _lib.ptr(ranks), _lib.ptr(rows),

@@ -185,6 +185,46 @@ def _(grad_1, B_1, grad_2, B_2, offsets, trans_b=True):
     return torch.empty((grad_1.shape[0], k), device=grad_1.device, dtype=grad_1.dtype)
 
 
+_SIDE = {}
+
+
+def side_stream(device: torch.device):
+    """A second stream per device for a backward GEMM that needs none of the others' outputs
+    (the down projection's wgrad), so its tiles can fill the SMs the input-gradient GEMM's
+    last wave of tiles leaves idle.  Opt-in (MOE_B200_BWD_STREAMS=1): on one GPU it measured
+    no gain (cfg4: 16.29 vs 16.26 ms per step); it targets steps with only a few waves of
+    tiles per GEMM (expert parallelism over many GPUs)."""
+    import os
+
+    if os.environ.get("MOE_B200_BWD_STREAMS", "0") != "1":
+        return None
+    key = torch.device(device).index
+    if key not in _SIDE:
+        _SIDE[key] = torch.cuda.Stream(device=device)
+    return _SIDE[key]
+
+
+def run_on_side(fn, device):
+    """fn() on the side stream after the current stream's work so far; returns (result,
+    join) where join() makes the current stream wait for it.  Without a side stream, fn()
+    runs here."""
+    side = side_stream(device)
+    if side is None:
+        out = fn()
+        return out, (lambda: None)
+    cur = torch.cuda.current_stream(device)
+    side.wait_stream(cur)
+    with torch.cuda.stream(side):
+        out = fn()
+
+    def join():
+        cur.wait_stream(side)
+        if out is not None:
+            out.record_stream(cur)
+
+    return out, join
+
+
 def _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b, needs):
     grad_A = grad_g = grad_u = None
     if needs[0]:
@@ -237,9 +277,12 @@ class GroupedSwiGLUMLP(torch.autograd.Function):
         trans_b = ctx.trans_b
         grad_out = grad_out.contiguous()
         dgate, dup = gmm_dgrad_swiglu_bwd_raw(grad_out, B_down, gate, up, offsets, trans_b)
-        grad_d = gmm_bwd_B_raw(h, B_down, offsets, grad_out, trans_b) if ctx.needs_input_grad[3] else None
+        grad_d, join = (run_on_side(lambda: gmm_bwd_B_raw(h, B_down, offsets, grad_out, trans_b),
+                                    grad_out.device)
+                        if ctx.needs_input_grad[3] else (None, lambda: None))
         grads = _gate_up_backward(A, B_gate, B_up, offsets, dgate, dup, trans_b,
                                   ctx.needs_input_grad[:3])
+        join()
         return (*grads, grad_d, None, None)
 
 
